@@ -1,0 +1,416 @@
+"""Benchmark of the paged decode path (KV append + decode attention, one layer).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload NAME]
+
+A step is one call of the north-star op on one batch: append the step's new
+K/V rows through slot_mapping, then paged decode attention over every
+sequence.  Default workload: BASELINE config 3 (Llama-3-8B shape, bf16,
+B=256, 32/8 heads, D=128, log-uniform context 256..8192) — the configuration
+the north-star target is quoted on.  Inputs are larger than L2 (~2.4 GB of KV
+per call), so no flush is needed between steps.
+
+Multi-GPU (torchrun, one process per GPU): sequences shard across ranks with
+no collective on the data path (greedy longest-first balancing of attended
+lengths); every rank holds 256 sequences' worth of work, so scaling is weak.
+Timing is on the device with CUDA events, bracketed by barrier + synchronize,
+max over ranks.
+
+Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
+algorithm (the C restatement in oracle/, all host threads) on a bounded row
+sample of the same workload instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "decode-attn tokens/s and achieved HBM GB/s (% peak) at 1/2/4/8 B200"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _peak_hbm() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during timing."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.lines: list[str] = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            ident = str(device_index)
+        self.cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                    "-lms", "200", "-i", ident]
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _traffic_from_profiles(workload: str) -> float | None:
+    """DRAM bytes per decode launch recorded from an ncu capture (profiles/*.md,
+    line 'dram_bytes_per_launch[<workload>]: <bytes>'), or None."""
+    for p in sorted((REPO / "profiles").glob("*.md")):
+        for line in p.read_text().splitlines():
+            key = f"dram_bytes_per_launch[{workload}]:"
+            if line.strip().startswith(key):
+                try:
+                    return float(line.split(":", 1)[1].strip().split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+def run_reference(args) -> None:
+    """CPU arm: the reference's CPU decode algorithm (oracle/pa_oracle.c, OpenMP
+    over rows, all host threads) + the append restatement, on a bounded sample."""
+    world, rank, _ = _dist_setup()
+    if rank != 0:
+        return
+    from llm_serving_runtime_b200.workloads import SPECS, make_workload, sample_lengths
+    from oracle import oracle
+
+    spec = SPECS[args.workload]
+    GB = spec.batch * world
+    lens_all = sample_lengths(spec, GB)
+    g = torch.Generator().manual_seed(4242)
+    n_sample = min(args.cpu_rows, GB)
+    rows = sorted(torch.randperm(GB, generator=g)[:n_sample].tolist())
+    w = make_workload(spec, device="cpu", rows=rows, global_batch=GB)
+    threads = os.cpu_count() or 1
+    kc, vc = w.key_cache.clone(), w.value_cache.clone()
+
+    def step():
+        oracle.kv_append(w.new_key, w.new_value, kc, vc, w.slot_mapping)
+        oracle.paged_decode(w.query, kc, vc, w.block_tables, w.context_lens, w.scale, num_threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    # scale the sample's time to the whole batch by attended tokens
+    L_all = float((lens_all + spec.q_len).sum())
+    L_smp = float((lens_all[rows] + spec.q_len).sum())
+    t_full = dt * L_all / L_smp
+    value = GB * spec.q_len / t_full
+    sample = (f"{n_sample} of {GB} sequences of {args.workload} (seeded), append + decode per step; "
+              f"time scaled to the full batch by attended tokens ({L_smp:.0f} of {L_all:.0f})")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_full * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16",
+                                                          torch.float32: "fp32"}[spec.dtype],
+        "data": "synthetic (seeded)",
+        "config": {"workload": args.workload, "global_batch": GB, "q_len": spec.q_len,
+                   "num_q_heads": spec.num_q_heads, "num_kv_heads": spec.num_kv_heads,
+                   "head_dim": spec.head_dim, "block_size": spec.block_size},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", default="cfg3-llama3-8b")
+    ap.add_argument("--cpu-rows", type=int, default=16, help="rows in the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch.distributed as dist
+
+    from llm_serving_runtime_b200 import paged_attention_decode
+    from llm_serving_runtime_b200.workloads import SPECS, algorithmic_bytes, lpt_partition, make_workload, \
+        sample_lengths
+
+    world, rank, local = _dist_setup()
+    if world != args.gpus:
+        args.gpus = world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    spec = SPECS[args.workload]
+    GB = spec.batch * world
+    lens = sample_lengths(spec, GB) + spec.q_len
+    if spec.length_dist == "prefix":
+        per_group = spec.batch // spec.prefix_groups
+        groups = [list(range(i, i + per_group)) for i in range(0, GB, per_group)]
+        shards = lpt_partition(lens, world, groups=groups)
+    else:
+        shards = lpt_partition(lens, world)
+    w = make_workload(spec, device=dev, rows=shards[rank], global_batch=GB)
+    B, q = w.batch, w.q_len
+    out = torch.empty_like(w.query)
+
+    def step():
+        paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                               w.slot_mapping, w.new_key, w.new_value, out=out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps of append + decode ----
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    local_ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([local_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    tokens_all = torch.tensor([B * q], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tokens_all)
+    tokens_per_step = float(tokens_all.item())
+    value = tokens_per_step / (ms_per_step / 1e3)
+    gpu_launches = 2 * args.steps  # pa_kv_append + pa_decode per step
+
+    # ---- decode kernel alone, for the roofline (events around each launch) ----
+    n_dec = max(20, min(args.steps, 100))
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(n_dec)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(n_dec)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(n_dec):
+        starts[i].record(stream)
+        paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                               out=out)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    dec_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    dec_bytes = algorithmic_bytes(w, include_append=False)
+    call_bytes = algorithmic_bytes(w, include_append=True)
+    achieved = dec_bytes / (dec_ms / 1e3) / 1e9
+    peak, peak_src = _peak_hbm()
+
+    # ---- end to end through the public API with host buffers ----
+    host = {k: getattr(w, k).cpu().pin_memory() for k in
+            ("query", "new_key", "new_value", "slot_mapping", "context_lens", "block_tables")}
+    dev_in = {k: torch.empty_like(getattr(w, k)) for k in host}
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = host_out.numel() * host_out.element_size()
+    n_e2e = max(10, min(args.steps, 100))
+
+    def e2e_step():
+        for k, v in host.items():
+            dev_in[k].copy_(v, non_blocking=True)
+        paged_attention_decode(dev_in["query"], w.key_cache, w.value_cache, dev_in["block_tables"],
+                               dev_in["context_lens"], w.scale, dev_in["slot_mapping"], dev_in["new_key"],
+                               dev_in["new_value"], out=out)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = tokens_per_step / (float(t.item()) / n_e2e / 1e3)
+
+    # ---- CPU baseline (rank 0, one GPU only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _cpu_baseline(w, spec, args.cpu_rows)
+
+    clk = clocks.summary()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    traffic = _traffic_from_profiles(args.workload)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[spec.dtype],
+        "data": "synthetic (seeded; random block placement)",
+        "config": {
+            "workload": args.workload, "global_batch": GB, "q_len": q, "num_q_heads": spec.num_q_heads,
+            "num_kv_heads": spec.num_kv_heads, "head_dim": spec.head_dim, "block_size": spec.block_size,
+            "context_lens": f"{spec.length_dist} [{spec.length_lo}, {spec.length_hi}]",
+            "parallelism": f"seq-shard{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (no flush)",
+            "bytes_per_call": call_bytes,
+        },
+        "hbm_gbs_per_call": call_bytes / (ms_per_step / 1e3) / 1e9,
+        "roofline": {
+            "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic, "peak_source": peak_src, "kernel": "pa::decode_mma_kernel",
+            "kernel_ms": dec_ms, "algorithmic_bytes": dec_bytes,
+        },
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": gpu_launches,
+        "clocks": clk,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def _cpu_baseline(w, spec, n_rows: int) -> dict:
+    """The oracle (C restatement of the reference's CPU decode, all host threads)
+    on a seeded row sample of the bench workload, scaled to the full batch."""
+    from oracle import oracle
+
+    g = torch.Generator().manual_seed(4242)
+    B = w.batch
+    rows = sorted(torch.randperm(B, generator=g)[:min(n_rows, B)].tolist())
+    q_len = w.q_len
+    bs = w.key_cache.shape[2]
+    rows_t = torch.tensor(rows, device=w.block_tables.device)
+    lens = w.context_lens[rows_t].to(torch.int64) + q_len
+    nblk = (lens + bs - 1) // bs
+    maxb = int(nblk.max())
+    ids, tables, c = [], torch.zeros(len(rows), maxb, dtype=torch.int32), 0
+    for i in range(len(rows)):
+        n = int(nblk[i])
+        ids.append(w.block_tables[rows_t[i], :n].to(torch.int64))
+        tables[i, :n] = torch.arange(c, c + n, dtype=torch.int32)
+        c += n
+    ids = torch.cat(ids)
+    kc, vc = w.key_cache[ids].cpu(), w.value_cache[ids].cpu()
+    qq, cl = w.query[rows_t].cpu(), w.context_lens[rows_t].cpu()
+    nk, nv = w.new_key[rows_t].cpu(), w.new_value[rows_t].cpu()
+    slots = oracle.slot_mapping_from_tables(tables, cl.to(torch.int64), q_len, bs)
+    threads = os.cpu_count() or 1
+    reps, t_tot = 0, 0.0
+    while t_tot < 5.0 and reps < 50:
+        t0 = time.perf_counter()
+        oracle.kv_append(nk, nv, kc, vc, slots)
+        oracle.paged_decode(qq, kc, vc, tables, cl, w.scale, num_threads=threads)
+        t_tot += time.perf_counter() - t0
+        reps += 1
+    dt = t_tot / reps
+    L_all = float(w.attended_lengths().sum())
+    L_smp = float(lens.sum())
+    value = B * q_len / (dt * L_all / L_smp)
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(rows)} of {B} sequences (seeded), append + decode, {reps} reps; "
+                      f"scaled to the full batch by attended tokens ({L_smp:.0f} of {L_all:.0f})"}
+
+
+if __name__ == "__main__":
+    main()

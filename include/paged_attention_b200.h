@@ -1,0 +1,180 @@
+/*
+ * paged_attention_b200.h — C ABI of the B200 (sm_100a) paged-attention decode path.
+ *
+ * Two operations make up one decode step of one transformer layer:
+ *
+ *   pa_kv_append  scatters the step's new K/V rows into the paged KV cache.
+ *                 Replaces the scatter loop of GpuKVBlockPool.write_tokens_batch
+ *                 (runtime/phase2/paged_kv_kernel.py:176-227) and, through the
+ *                 slot_mapping form, the north-star `slot_mapping` argument.
+ *   pa_decode     attends every query row of every sequence over that sequence's
+ *                 blocks, reached through its block table.  Replaces
+ *                 _paged_attention_decode_batched_triton and its Triton kernels
+ *                 (runtime/phase2/paged_attention_triton.py:148-243, 245-336,
+ *                 338-412, 414-457, 460-660).
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless the name says host.  The library
+ *     never allocates device memory; the caller owns every buffer.
+ *   - Strides are in ELEMENTS.  The innermost (head_dim) stride is always 1.
+ *   - `stream` is a cudaStream_t passed as void*; every launch goes on it.
+ *   - Every function returns a pa_status (0 = PA_OK).  pa_last_error() gives a
+ *     human-readable reason for the last failure on the calling host thread.
+ *   - Device-detected input errors (a block id outside the pool, a sequence
+ *     longer than its block table, a slot outside the pool) never fault: the
+ *     kernel skips the access and ORs a PA_DEVERR_* bit into the status word at
+ *     the start of the workspace (or into `error_flags` for pa_kv_append).
+ *     pa_read_device_errors() reads it back.
+ *   - Launch-time work is graph-capture safe: no host synchronisation, no
+ *     allocation, grid sizes depend only on host-side shapes.
+ */
+#ifndef PAGED_ATTENTION_B200_H_
+#define PAGED_ATTENTION_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PA_API __attribute__((visibility("default")))
+#else
+#define PA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host) -------------------------------------------------- */
+typedef enum pa_status {
+  PA_OK = 0,
+  PA_ERR_INVALID_ARGUMENT = 1, /* bad shape / stride / null pointer  -> ValueError  */
+  PA_ERR_UNSUPPORTED = 2,      /* valid but not implemented (head_dim, block size) -> ValueError */
+  PA_ERR_WORKSPACE = 3,        /* workspace missing or too small      -> RuntimeError */
+  PA_ERR_CUDA = 4,             /* CUDA runtime / launch failure       -> RuntimeError */
+  PA_ERR_DEVICE = 5            /* device error word non-zero          -> IndexError   */
+} pa_status;
+
+/* ---- element types -------------------------------------------------------- */
+typedef enum pa_dtype {
+  PA_DTYPE_FLOAT32 = 0,
+  PA_DTYPE_FLOAT16 = 1,
+  PA_DTYPE_BFLOAT16 = 2
+} pa_dtype;
+
+/* ---- device error bits (status word / error_flags) ------------------------ */
+#define PA_DEVERR_BLOCK_ID_RANGE 0x1u /* block-table entry outside [0, num_blocks)       */
+#define PA_DEVERR_TABLE_UNDERRUN 0x2u /* sequence needs more blocks than max_blocks      */
+#define PA_DEVERR_SLOT_RANGE 0x4u     /* slot_mapping entry outside the pool             */
+#define PA_DEVERR_WAIT_TIMEOUT 0x8u   /* a bounded wait on a bulk copy ran out           */
+
+/* A paged cache view: [num_blocks, num_kv_heads, block_size, head_dim], head_dim
+ * contiguous.  For GpuKVBlockPool's per-layer view (paged_kv_kernel.py:124-134)
+ * stride_block = num_layers * num_kv_heads * block_size * head_dim. */
+typedef struct pa_cache_view {
+  void* data;
+  int64_t num_blocks;
+  int64_t stride_block;
+  int64_t stride_head;
+  int64_t stride_token;
+} pa_cache_view;
+
+/* Arguments of pa_kv_append.
+ * New rows `key`/`value` are [batch, num_kv_heads, q_len, head_dim] (HF layout).
+ * Token i = b * q_len + t is written to
+ *   slot = slot_mapping[i]                                 (slot_mapping != NULL)
+ *   slot = block_tables[b, p / bs] * bs + p % bs,
+ *          p = positions[b] + position_offset + t                      (otherwise)
+ * and lands in cache[slot / bs, h, slot % bs, :].  A negative slot_mapping entry
+ * marks a padding token and is skipped. */
+typedef struct pa_kv_append_args {
+  const void* key;
+  int64_t key_stride_b, key_stride_h, key_stride_t;
+  const void* value;
+  int64_t value_stride_b, value_stride_h, value_stride_t;
+  pa_cache_view key_cache;
+  pa_cache_view value_cache;
+  const int64_t* slot_mapping;  /* [batch * q_len] or NULL */
+  const int32_t* block_tables;  /* [batch, >= max_blocks] (used when slot_mapping == NULL) */
+  int64_t block_table_stride;
+  int32_t max_blocks;
+  const void* positions;        /* [batch] start position of token t=0 (slot_mapping == NULL) */
+  int32_t positions_is_int64;   /* 0: int32, 1: int64 */
+  int32_t position_offset;      /* added to every position (e.g. -q_len for post-append lengths) */
+  int32_t batch, q_len, num_kv_heads, head_dim, block_size;
+  int32_t dtype;                /* pa_dtype of key, value and both caches */
+  uint32_t* error_flags;        /* device word that receives PA_DEVERR_* bits (may be NULL) */
+} pa_kv_append_args;
+
+/* Arguments of pa_decode.
+ * query [batch, num_q_heads, q_len, head_dim]; out has the same shape and dtype.
+ * Sequence b attends L_b = context_lens[b] + len_offset tokens.  Query token t of
+ * row b sits at absolute position L_b - q_len + t and attends positions
+ * 0 .. L_b - q_len + t (causal over the q_len new tokens; q_len = 1 is plain decode).
+ * Query head hq reads KV head hq / (num_q_heads / num_kv_heads).
+ *   len_offset = q_len : context_lens counts the tokens cached BEFORE this step;
+ *   len_offset = 0     : context_lens already includes them (the reference's
+ *                        seq_lens, paged_attention_triton.py:50). */
+typedef struct pa_decode_args {
+  const void* query;
+  int64_t query_stride_b, query_stride_h, query_stride_t;
+  pa_cache_view key_cache;
+  pa_cache_view value_cache;
+  const int32_t* block_tables;  /* [batch, >= max_blocks] */
+  int64_t block_table_stride;
+  int32_t max_blocks;
+  const int32_t* context_lens;  /* [batch] */
+  int32_t len_offset;
+  void* out;
+  int64_t out_stride_b, out_stride_h, out_stride_t;
+  int32_t batch, q_len, num_q_heads, num_kv_heads, head_dim, block_size;
+  int32_t dtype;                /* pa_dtype of query, caches and out */
+  float scale;                  /* softmax scale applied to q.k */
+  void* workspace;              /* device scratch, pa_decode_workspace_bytes() long,
+                                   zero-filled once before first use (pa_workspace_init) */
+  size_t workspace_bytes;
+  int32_t allow_overlap_with_previous; /* 1: programmatic dependent launch on the kernel
+                                          launched just before on `stream` (pa_kv_append) */
+} pa_decode_args;
+
+/* Scatter new K/V rows into the paged cache.  Bit-exact copy.
+ * Replaces: GpuKVBlockPool.write_tokens_batch, runtime/phase2/paged_kv_kernel.py:176-227
+ * (and write_tokens :136-174, which delegates to it for batch 1). */
+PA_API int pa_kv_append(const pa_kv_append_args* args, void* stream);
+
+/* Paged decode attention (split-K over the whole batch with an in-kernel
+ * log-sum-exp merge).  fp16/bf16 use tensor-core tiles; fp32 stays on CUDA cores.
+ * Replaces: paged_attention_decode_batched -> _paged_attention_decode_batched_triton,
+ * runtime/phase2/paged_attention_triton.py:460-552 and :745-775, with the kernels at
+ * :148-243 (direct batched), :245-336 (split), :338-412 (direct single) and
+ * :414-457 (log-sum-exp combine). */
+PA_API int pa_decode(const pa_decode_args* args, void* stream);
+
+/* Bytes of workspace pa_decode needs on `device` for these shapes.
+ * Replaces the scratch caches _decode_scratch_buffers / _direct_out_buffer
+ * (runtime/phase2/paged_attention_triton.py:90-115); unlike them the output is
+ * never aliased to scratch. */
+PA_API size_t pa_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                 int32_t q_len, int32_t head_dim, int32_t dtype, int32_t device);
+
+/* Zero a workspace (its merge counters and status word) on `stream`.  Needed
+ * once after allocation; pa_decode leaves the counters at zero after each call.
+ * No counterpart in the reference (its scratch needs no initialisation). */
+PA_API int pa_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Copy the device status word at the start of `workspace` (or any device
+ * uint32 word) to *host_flags, optionally clearing it.  Synchronises `stream`.
+ * Stands in for the host-side checks that raise IndexError in the reference
+ * (paged_kv_kernel.py:118-119, :167-170, :221-222). */
+PA_API int pa_read_device_errors(void* device_word, uint32_t* host_flags, int32_t clear, void* stream);
+
+/* Text for the last failure on this host thread ("" when none). */
+PA_API const char* pa_last_error(void);
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+PA_API int32_t pa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGED_ATTENTION_B200_H_ */

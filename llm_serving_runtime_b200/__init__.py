@@ -1,0 +1,25 @@
+"""B200-native (sm_100a) paged-attention decode path of llm-serving-runtime.
+
+Public entry points
+  paged_attention_decode(query, key_cache, value_cache, block_tables,
+                         context_lens, scale, slot_mapping=None, key=None, value=None)
+      the north-star call: fused KV append + paged decode attention
+  kv_append(...)                      the KV-append kernel alone
+  reference_api                       drop-in for runtime/phase2/paged_attention_triton.py
+  kv_block_pool.GpuKVBlockPool        drop-in for runtime/phase2/paged_kv_kernel.py
+  block_paged_attention               drop-in HF attention hook
+  integration.install()               patch the reference runtime in place
+
+The kernels live in lib/libpa_b200.so (C ABI: include/paged_attention_b200.h).
+"""
+
+from .paged_attention import (  # noqa: F401
+    DeviceErrorFlags,
+    decode_workspace,
+    describe_device_errors,
+    kv_append,
+    paged_attention_decode,
+    read_device_errors,
+)
+
+__version__ = "1.0.0"

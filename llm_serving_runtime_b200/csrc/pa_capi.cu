@@ -1,0 +1,383 @@
+// pa_capi.cu — the extern "C" boundary of the paged-decode library.
+//
+// Validates arguments (returning PA_ERR_* with a message, never aborting),
+// encodes the TMA tensor maps of the two caches, sizes the grid from the
+// device's SM count (never from device data, so calls are graph-capture safe)
+// and launches the kernels on the caller's stream.  Nothing here allocates.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "pa_common.cuh"
+#include "pa_internal.h"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+  int num_sms = 0;
+  int max_smem_optin = 0;
+  bool prepared[3][2] = {{false, false}, {false, false}, {false, false}};  // [dtype][D==128]
+  size_t prepared_smem[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+};
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+bool g_dev_valid[kMaxDevices] = {false};
+std::mutex g_mu;
+
+int device_info(int dev, DeviceInfo** out) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(PA_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_dev_valid[dev]) {
+    cudaError_t e = cudaDeviceGetAttribute(&g_dev[dev].num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    e = cudaDeviceGetAttribute(&g_dev[dev].max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(smem opt-in)");
+    g_dev_valid[dev] = true;
+  }
+  *out = &g_dev[dev];
+  return PA_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encode(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_encode == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || ptr == nullptr)
+      return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  *fn = g_encode;
+  return PA_OK;
+}
+
+int elem_bytes(int dtype) { return dtype == PA_DTYPE_FLOAT32 ? 4 : 2; }
+
+bool aligned_ptr(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+int check_cache_view(const pa_cache_view& v, const char* name) {
+  if (v.data == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "%s: null data pointer", name);
+  if (v.num_blocks <= 0) return fail(PA_ERR_INVALID_ARGUMENT, "%s: num_blocks must be positive", name);
+  if (v.stride_block <= 0 || v.stride_head <= 0 || v.stride_token <= 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "%s: strides must be positive", name);
+  return PA_OK;
+}
+
+// 4-D tensor map (head_dim, token, kv head, block) with 128-byte swizzle and a
+// box of (64 elements, min(bs, 16) tokens, 1, 1).
+int encode_cache_map(CUtensorMap* map, const pa_cache_view& v, int dtype, int D, int bs, int Hkv,
+                     const char* name) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  int st = get_encode(&enc);
+  if (st != PA_OK) return st;
+  const int e = elem_bytes(dtype);
+  if (!aligned_ptr(v.data, 16))
+    return fail(PA_ERR_UNSUPPORTED, "%s: base address must be 16-byte aligned", name);
+  const int64_t sb[3] = {v.stride_token * e, v.stride_head * e, v.stride_block * e};
+  for (int i = 0; i < 3; ++i)
+    if (sb[i] % 16 != 0 || sb[i] >= (int64_t(1) << 40))
+      return fail(PA_ERR_UNSUPPORTED, "%s: strides must be multiples of 16 bytes", name);
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)bs, (cuuint64_t)Hkv, (cuuint64_t)v.num_blocks};
+  cuuint64_t strides[3] = {(cuuint64_t)sb[0], (cuuint64_t)sb[1], (cuuint64_t)sb[2]};
+  cuuint32_t box[4] = {64u, (cuuint32_t)(bs < 16 ? bs : 16), 1u, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = enc(map, dtype == PA_DTYPE_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   4, v.data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PA_ERR_UNSUPPORTED, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return PA_OK;
+}
+
+struct DecodeShape {
+  int G, GQ, NMG, slot_rows;
+};
+
+DecodeShape decode_shape(int Hq, int Hkv, int q_len) {
+  DecodeShape s;
+  s.G = Hq / Hkv;
+  s.GQ = s.G * q_len;
+  s.NMG = (s.GQ + 15) / 16;
+  s.slot_rows = s.GQ < 16 ? s.GQ : 16;
+  return s;
+}
+
+size_t workspace_bytes_impl(int B, int Hkv, int NMG, int slot_rows, int D, int nw_total) {
+  return pa::kWsHeaderBytes + pa::ws_counter_bytes(B, Hkv, NMG) +
+         pa::ws_partial_bytes(nw_total, slot_rows, D);
+}
+
+}  // namespace
+
+namespace pa {
+
+size_t ws_counter_bytes(int B, int Hkv, int NMG) { return round_up((size_t)B * Hkv * NMG * 4); }
+
+size_t ws_partial_bytes(int nw_total, int slot_rows, int D) {
+  return round_up((size_t)2 * nw_total * slot_rows * (2 + D) * 4);
+}
+
+}  // namespace pa
+
+extern "C" {
+
+const char* pa_last_error(void) { return g_last_error; }
+
+int32_t pa_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+
+size_t pa_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                 int32_t q_len, int32_t head_dim, int32_t dtype, int32_t device) {
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || q_len <= 0 || head_dim <= 0 ||
+      num_q_heads % num_kv_heads != 0)
+    return 0;
+  DeviceInfo* info = nullptr;
+  if (device_info(device, &info) != PA_OK) return 0;
+  const DecodeShape s = decode_shape(num_q_heads, num_kv_heads, q_len);
+  if (dtype == PA_DTYPE_FLOAT32) return pa::kWsHeaderBytes;
+  return workspace_bytes_impl(batch, num_kv_heads, s.NMG, s.slot_rows, head_dim,
+                              info->num_sms * pa::kDecodeWarps);
+}
+
+int pa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error[0] = 0;
+  if (workspace == nullptr || workspace_bytes < pa::kWsHeaderBytes)
+    return fail(PA_ERR_WORKSPACE, "workspace must be at least %zu bytes", pa::kWsHeaderBytes);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+  return PA_OK;
+}
+
+int pa_read_device_errors(void* device_word, uint32_t* host_flags, int32_t clear, void* stream) {
+  g_last_error[0] = 0;
+  if (device_word == nullptr || host_flags == nullptr)
+    return fail(PA_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(host_flags, device_word, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(status word)");
+  if (clear) {
+    e = cudaMemsetAsync(device_word, 0, sizeof(uint32_t), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status word)");
+  }
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  return PA_OK;
+}
+
+int pa_kv_append(const pa_kv_append_args* a, void* stream) {
+  g_last_error[0] = 0;
+  if (a == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null args");
+  if (a->dtype < PA_DTYPE_FLOAT32 || a->dtype > PA_DTYPE_BFLOAT16)
+    return fail(PA_ERR_UNSUPPORTED, "unsupported dtype %d", a->dtype);
+  if (a->batch < 0 || a->q_len <= 0 || a->num_kv_heads <= 0 || a->head_dim <= 0 || a->block_size <= 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "batch/q_len/num_kv_heads/head_dim/block_size must be positive");
+  if (a->batch == 0) return PA_OK;
+  if (a->key == nullptr || a->value == nullptr)
+    return fail(PA_ERR_INVALID_ARGUMENT, "key and value must be given");
+  int st = check_cache_view(a->key_cache, "key_cache");
+  if (st != PA_OK) return st;
+  st = check_cache_view(a->value_cache, "value_cache");
+  if (st != PA_OK) return st;
+  if (a->key_cache.num_blocks != a->value_cache.num_blocks)
+    return fail(PA_ERR_INVALID_ARGUMENT, "key_cache and value_cache must have the same number of blocks");
+  if (a->slot_mapping == nullptr) {
+    if (a->block_tables == nullptr || a->positions == nullptr)
+      return fail(PA_ERR_INVALID_ARGUMENT, "without slot_mapping, block_tables and positions are required");
+    if (a->max_blocks <= 0) return fail(PA_ERR_INVALID_ARGUMENT, "max_blocks must be positive");
+  }
+  pa::AppendParams p;
+  p.key = a->key;
+  p.k_sb = a->key_stride_b;
+  p.k_sh = a->key_stride_h;
+  p.k_st = a->key_stride_t;
+  p.value = a->value;
+  p.v_sb = a->value_stride_b;
+  p.v_sh = a->value_stride_h;
+  p.v_st = a->value_stride_t;
+  p.k_cache = a->key_cache.data;
+  p.kc_sblk = a->key_cache.stride_block;
+  p.kc_sh = a->key_cache.stride_head;
+  p.kc_st = a->key_cache.stride_token;
+  p.v_cache = a->value_cache.data;
+  p.vc_sblk = a->value_cache.stride_block;
+  p.vc_sh = a->value_cache.stride_head;
+  p.vc_st = a->value_cache.stride_token;
+  p.num_blocks = a->key_cache.num_blocks;
+  p.slot_mapping = a->slot_mapping;
+  p.block_tables = a->block_tables;
+  p.bt_stride = a->block_table_stride;
+  p.max_blocks = a->max_blocks;
+  p.positions = a->positions;
+  p.positions_is_int64 = a->positions_is_int64;
+  p.position_offset = a->position_offset;
+  p.B = a->batch;
+  p.q_len = a->q_len;
+  p.Hkv = a->num_kv_heads;
+  p.D = a->head_dim;
+  p.bs = a->block_size;
+  p.elem_bytes = elem_bytes(a->dtype);
+  p.error_flags = a->error_flags;
+  cudaError_t e = pa::launch_kv_append(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+  return PA_OK;
+}
+
+int pa_decode(const pa_decode_args* a, void* stream) {
+  g_last_error[0] = 0;
+  if (a == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null args");
+  const int dtype = a->dtype;
+  if (dtype < PA_DTYPE_FLOAT32 || dtype > PA_DTYPE_BFLOAT16)
+    return fail(PA_ERR_UNSUPPORTED, "unsupported dtype %d", dtype);
+  if (a->batch < 0 || a->q_len <= 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0 ||
+      a->head_dim <= 0 || a->block_size <= 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "batch/q_len/heads/head_dim/block_size must be positive");
+  if (a->num_q_heads % a->num_kv_heads != 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "num_q_heads (%d) must be a multiple of num_kv_heads (%d)",
+                a->num_q_heads, a->num_kv_heads);
+  if (a->batch == 0) return PA_OK;
+  if (a->query == nullptr || a->out == nullptr || a->block_tables == nullptr || a->context_lens == nullptr)
+    return fail(PA_ERR_INVALID_ARGUMENT, "query, out, block_tables and context_lens must be given");
+  if (a->max_blocks <= 0) return fail(PA_ERR_INVALID_ARGUMENT, "max_blocks must be positive");
+  int st = check_cache_view(a->key_cache, "key_cache");
+  if (st != PA_OK) return st;
+  st = check_cache_view(a->value_cache, "value_cache");
+  if (st != PA_OK) return st;
+  if (a->key_cache.num_blocks != a->value_cache.num_blocks)
+    return fail(PA_ERR_INVALID_ARGUMENT, "key_cache and value_cache must have the same number of blocks");
+  const int D = a->head_dim, bs = a->block_size;
+  if ((int64_t)a->max_blocks * bs > (int64_t)1 << 30)
+    return fail(PA_ERR_UNSUPPORTED, "max_blocks * block_size too large");
+  if (!aligned_ptr(a->query, 4) || !aligned_ptr(a->out, 4) ||
+      ((a->query_stride_b | a->query_stride_h | a->query_stride_t | a->out_stride_b |
+        a->out_stride_h | a->out_stride_t) & 1) != 0)
+    return fail(PA_ERR_UNSUPPORTED, "query/out rows must be 4-byte aligned");
+  if (a->workspace == nullptr || a->workspace_bytes < pa::kWsHeaderBytes)
+    return fail(PA_ERR_WORKSPACE, "a workspace of pa_decode_workspace_bytes() bytes is required");
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceInfo* info = nullptr;
+  st = device_info(dev, &info);
+  if (st != PA_OK) return st;
+
+  const DecodeShape s = decode_shape(a->num_q_heads, a->num_kv_heads, a->q_len);
+  pa::DecodeParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = a->query;
+  p.q_sb = a->query_stride_b;
+  p.q_sh = a->query_stride_h;
+  p.q_st = a->query_stride_t;
+  p.k_cache = a->key_cache.data;
+  p.v_cache = a->value_cache.data;
+  p.k_sblk = a->key_cache.stride_block;
+  p.k_sh = a->key_cache.stride_head;
+  p.k_st = a->key_cache.stride_token;
+  p.v_sblk = a->value_cache.stride_block;
+  p.v_sh = a->value_cache.stride_head;
+  p.v_st = a->value_cache.stride_token;
+  p.num_blocks = a->key_cache.num_blocks;
+  p.block_tables = a->block_tables;
+  p.bt_stride = a->block_table_stride;
+  p.max_blocks = a->max_blocks;
+  p.context_lens = a->context_lens;
+  p.len_offset = a->len_offset;
+  p.out = a->out;
+  p.o_sb = a->out_stride_b;
+  p.o_sh = a->out_stride_h;
+  p.o_st = a->out_stride_t;
+  p.B = a->batch;
+  p.q_len = a->q_len;
+  p.Hq = a->num_q_heads;
+  p.Hkv = a->num_kv_heads;
+  p.G = s.G;
+  p.GQ = s.GQ;
+  p.NMG = s.NMG;
+  p.bs = bs;
+  p.D = D;
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.status = static_cast<uint32_t*>(a->workspace);
+  p.slot_rows = s.slot_rows;
+  const bool pdl = a->allow_overlap_with_previous != 0;
+  cudaStream_t strm = static_cast<cudaStream_t>(stream);
+
+  if (dtype == PA_DTYPE_FLOAT32) {
+    if (D != 32 && D != 64 && D != 128 && D != 256)
+      return fail(PA_ERR_UNSUPPORTED, "fp32 decode supports head_dim 32/64/128/256, got %d", D);
+    if (!aligned_ptr(a->key_cache.data, 4) || !aligned_ptr(a->value_cache.data, 4))
+      return fail(PA_ERR_UNSUPPORTED, "cache base must be 4-byte aligned");
+    e = pa::launch_decode_f32(p, pdl, strm);
+    if (e != cudaSuccess) return cuda_fail(e, "decode_f32 launch");
+    return PA_OK;
+  }
+
+  // fp16 / bf16: tensor-core kernel.
+  if (D != 64 && D != 128)
+    return fail(PA_ERR_UNSUPPORTED, "fp16/bf16 decode supports head_dim 64/128, got %d", D);
+  if (bs < 8 || bs > 256 || (bs & (bs - 1)) != 0)
+    return fail(PA_ERR_UNSUPPORTED, "fp16/bf16 decode needs a power-of-two block_size in [8, 256], got %d", bs);
+  const int grid = info->num_sms;
+  p.nw_total = grid * pa::kDecodeWarps;
+  const size_t need = workspace_bytes_impl(p.B, p.Hkv, p.NMG, p.slot_rows, D, p.nw_total);
+  if (a->workspace_bytes < need)
+    return fail(PA_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", a->workspace_bytes, need);
+  char* ws = static_cast<char*>(a->workspace);
+  p.counters = reinterpret_cast<int32_t*>(ws + pa::kWsHeaderBytes);
+  p.partials = reinterpret_cast<float*>(ws + pa::kWsHeaderBytes + pa::ws_counter_bytes(p.B, p.Hkv, p.NMG));
+
+  // Ring depth: as many 16-token stages per warp as shared memory allows (2..8).
+  const size_t budget = (size_t)info->max_smem_optin - 64;  // static shared memory of the kernel
+  int stages = 8;
+  while (stages >= 2 && pa::decode_mma_smem_bytes(D, p.B, stages) > budget) --stages;
+  if (stages < 2)
+    return fail(PA_ERR_UNSUPPORTED, "batch %d too large for the decode kernel's shared memory", p.B);
+  p.stages = stages;
+  const size_t smem = pa::decode_mma_smem_bytes(D, p.B, stages);
+
+  CUtensorMap tmk, tmv;
+  st = encode_cache_map(&tmk, a->key_cache, dtype, D, bs, p.Hkv, "key_cache");
+  if (st != PA_OK) return st;
+  st = encode_cache_map(&tmv, a->value_cache, dtype, D, bs, p.Hkv, "value_cache");
+  if (st != PA_OK) return st;
+
+  {
+    const int di = dtype, dj = D == 128 ? 1 : 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!info->prepared[di][dj] || info->prepared_smem[di][dj] < smem) {
+      e = pa::decode_mma_prepare(dtype, D, smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+      info->prepared[di][dj] = true;
+      info->prepared_smem[di][dj] = smem;
+    }
+  }
+  e = pa::launch_decode_mma(p, tmk, tmv, dtype, grid, smem, pdl, strm);
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return PA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,597 @@
+// pa_decode_mma.cu — paged decode attention for fp16 / bf16 on sm_100a.
+//
+// What it computes (per sequence b, KV head h, query row (g, t)):
+//   out[b, h*G+g, t, :] = softmax_j( q . k_j * scale ) @ v_j   over cached tokens
+//   j = 0 .. L_b - q_len + t  (causal over the q_len new tokens; q_len = 1: all L_b)
+// which is the math of the reference's decode kernels and CPU path
+// (runtime/phase2/paged_attention_triton.py:148-243 and :663-704): fp32 scores,
+// online softmax with running max m, sum l and accumulator acc, out = acc / l.
+//
+// How (B200-first):
+//  * Work is one flat list of 16-token "units" ordered (sequence, kv head,
+//    query-row group, unit).  Every warp of the persistent grid takes an equal,
+//    contiguous slice of it (stream-K), so ragged / log-uniform lengths balance
+//    to within one unit.  A slice that covers a whole (sequence, head) writes
+//    the output directly; a row cut by a slice boundary leaves (m, l, acc)
+//    partials in the workspace, and the last warp to finish that row merges
+//    them with a log-sum-exp reduction (arrival counter, reset after use).
+//  * GQA packing: the G query heads (times q_len query tokens) that read one KV
+//    head form the 16 rows of an m16n8k16 tile, so each K/V tile is read from
+//    HBM once for the whole group.
+//  * Each warp is a self-fed engine: its lane 0 issues 4-D TMA tile loads
+//    (128-byte swizzle, no multicast) of the unit's K and V tiles into a ring of
+//    `stages` shared-memory slots tracked by mbarriers; the warp keeps `stages`
+//    units in flight while it computes the oldest one.  Block-table entries are
+//    fetched 32 at a time with one coalesced load and shuffled to lane 0.
+//  * QK^T and PV run on tensor cores (ldmatrix + mma.sync m16n8k16, fp32
+//    accumulate); the online softmax uses quad shuffles and ex2.
+#include <math.h>
+
+#include "pa_common.cuh"
+#include "pa_internal.h"
+
+namespace pa {
+
+namespace {
+
+struct Cursor {
+  int b;  // sequence
+  int r;  // row within the sequence: kv_head * NMG + m-group
+  int u;  // unit within the row
+  int n;  // units in the row
+};
+
+}  // namespace
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kDecodeWarps * 32, 1)
+    decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                      const DecodeParams p) {
+  constexpr int KSTEPS = D / 16;             // k-steps of QK^T
+  constexpr int NDT = D / 8;                 // n-tiles of PV
+  constexpr int HALVES = D / 64;             // 128-byte column halves of a tile row
+  constexpr uint32_t TILE_BYTES = 16 * D * 2;  // one 16-token K (or V) tile
+  constexpr uint32_t STAGE_BYTES = 2 * TILE_BYTES;
+  constexpr int DPL = D / 32;                // dims per lane in the merge
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const int stages = p.stages;
+  const uint32_t ring_addr = smem_addr(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kDecodeWarps * stages * STAGE_BYTES);
+  int* s_lens = reinterpret_cast<int*>(bars + kDecodeWarps * stages);
+  int* s_pref = s_lens + p.B;
+  __shared__ int s_warp_tot[kDecodeWarps];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int B = p.B;
+
+  if (lane == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(smem_addr(&bars[warp * stages + s]), 1);
+  }
+  if (tid == 0) {
+    prefetch_tensormap(&tmk);
+    prefetch_tensormap(&tmv);
+  }
+
+  // ---- prologue: attended lengths and the exclusive prefix of units per sequence.
+  // (context_lens and block tables are not written by the append kernel, so
+  // this runs before griddepcontrol.wait and overlaps it.)
+  {
+    const int cap = p.max_blocks * p.bs;
+    const int nthr = (int)blockDim.x;
+    const int per = (B + nthr - 1) / nthr;
+    const int beg = min(B, tid * per);
+    const int end = min(B, beg + per);
+    int local = 0;
+    for (int b = beg; b < end; ++b) {
+      int L = p.context_lens[b] + p.len_offset;
+      if (L > cap) {
+        if (blockIdx.x == 0) raise_flag(p.status, PA_DEVERR_TABLE_UNDERRUN);
+        L = cap;
+      }
+      if (L < 0) L = 0;
+      s_lens[b] = L;
+      local += (L + kUnitTokens - 1) / kUnitTokens;
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_warp_tot[warp] = incl;
+    __syncthreads();
+    int run = incl - local;
+    for (int w = 0; w < warp; ++w) run += s_warp_tot[w];
+    for (int b = beg; b < end; ++b) {
+      s_pref[b] = run;
+      run += (s_lens[b] + kUnitTokens - 1) / kUnitTokens;
+    }
+    if (tid == nthr - 1) s_pref[B] = run;
+  }
+  fence_mbar_init();
+  __syncthreads();
+
+  // Sequences with nothing to attend produce zeros (their rows get no unit).
+  for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    if (s_lens[b] != 0) continue;
+    const int rows = p.Hq * p.q_len;
+    for (int i = tid; i < rows * (D / 2); i += blockDim.x) {
+      const int row = i / (D / 2);
+      const int d2 = i - row * (D / 2);
+      const int head = row / p.q_len;
+      const int t = row - head * p.q_len;
+      T* o = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)head * p.o_sh +
+             (long long)t * p.o_st + 2 * d2;
+      *reinterpret_cast<uint32_t*>(o) = 0u;
+    }
+  }
+
+  // Everything below reads the KV cache, which the previous kernel may write.
+  pdl_wait_previous();
+
+  const int rows_per_b = p.Hkv * p.NMG;
+  const long long W = (long long)rows_per_b * s_pref[B];
+  if (W == 0) return;
+  long long nw_eff = (W + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
+  if (nw_eff > p.nw_total) nw_eff = p.nw_total;
+  if (nw_eff < 1) nw_eff = 1;
+  const int gw = blockIdx.x * kDecodeWarps + warp;
+  if (gw >= nw_eff) return;
+  const long long ws = W * gw / nw_eff;
+  const long long we = W * (gw + 1) / nw_eff;
+  if (ws >= we) return;
+
+  // Locate the first unit of this warp's slice.
+  Cursor start;
+  {
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if ((long long)rows_per_b * s_pref[mid] <= ws)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    start.b = lo;
+    start.n = s_pref[lo + 1] - s_pref[lo];
+    const long long off = ws - (long long)rows_per_b * s_pref[lo];
+    start.r = (int)(off / start.n);
+    start.u = (int)(off - (long long)start.r * start.n);
+  }
+  auto advance = [&](Cursor& c) {
+    if (++c.u == c.n) {
+      c.u = 0;
+      if (++c.r == rows_per_b) {
+        c.r = 0;
+        do {
+          ++c.b;
+        } while (c.b < B && s_pref[c.b + 1] == s_pref[c.b]);
+        if (c.b < B) c.n = s_pref[c.b + 1] - s_pref[c.b];
+      }
+    }
+  };
+
+  const uint32_t my_ring = ring_addr + (uint32_t)(warp * stages) * STAGE_BYTES;
+  const uint32_t my_bars = smem_addr(&bars[warp * stages]);
+
+  // ---- producer (lane 0 issues; the warp shares the block-table window) ----
+  Cursor pc = start;
+  long long pf = ws;
+  int win_b = -1, win_base = 0, win_val = -1;
+  const int bs = p.bs;
+
+  // Keeps block-table entries [win_base, win_base + 32) of sequence win_b in
+  // the warp's lanes; reloads (one coalesced load) when lb .. lb+need-1 leave it.
+  auto ensure_window = [&](int b, int lb, int need) {
+    if (b != win_b || lb < win_base || lb + need > win_base + 32) {
+      win_b = b;
+      win_base = lb;
+      const int e = lb + lane;
+      win_val = (e < p.max_blocks) ? __ldg(&p.block_tables[(long long)b * p.bt_stride + e]) : -1;
+    }
+  };
+
+  auto issue = [&](int slot) {
+    const int h = pc.r / p.NMG;
+    const uint32_t stage = my_ring + (uint32_t)slot * STAGE_BYTES;
+    const uint32_t bar = my_bars + (uint32_t)slot * 8u;
+    const int tok0 = pc.u * kUnitTokens;
+    if (bs >= kUnitTokens) {
+      const int lb = tok0 / bs;
+      const int y = tok0 - lb * bs;
+      ensure_window(pc.b, lb, 1);
+      const int phys = __shfl_sync(0xffffffffu, win_val, lb - win_base);
+      if (lane == 0) {
+        if (phys < 0 || phys >= p.num_blocks) raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
+        mbar_arrive_expect_tx(bar, STAGE_BYTES);
+#pragma unroll
+        for (int hf = 0; hf < HALVES; ++hf)
+          tma_load_4d(stage + hf * 2048u, &tmk, bar, hf * 64, y, h, phys);
+#pragma unroll
+        for (int hf = 0; hf < HALVES; ++hf)
+          tma_load_4d(stage + TILE_BYTES + hf * 2048u, &tmv, bar, hf * 64, y, h, phys);
+      }
+    } else {
+      // Block size 8: two blocks per unit; a block past the sequence end is not loaded.
+      const int L = s_lens[pc.b];
+      const int lb0 = tok0 / bs;
+      ensure_window(pc.b, lb0, 2);
+      const int phys0 = __shfl_sync(0xffffffffu, win_val, lb0 - win_base);
+      const int phys1 = __shfl_sync(0xffffffffu, win_val, lb0 + 1 - win_base);
+      if (lane == 0) {
+        const bool need1 = (lb0 + 1) * bs < L;
+        const uint32_t box_bytes = (uint32_t)bs * 128u;
+        const uint32_t nbox = (need1 ? 2u : 1u) * HALVES * 2u;
+        if (phys0 < 0 || phys0 >= p.num_blocks || (need1 && (phys1 < 0 || phys1 >= p.num_blocks)))
+          raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
+        mbar_arrive_expect_tx(bar, nbox * box_bytes);
+        for (int j = 0; j < (need1 ? 2 : 1); ++j) {
+          const int phys = j ? phys1 : phys0;
+#pragma unroll
+          for (int hf = 0; hf < HALVES; ++hf) {
+            tma_load_4d(stage + hf * 2048u + j * box_bytes, &tmk, bar, hf * 64, 0, h, phys);
+            tma_load_4d(stage + TILE_BYTES + hf * 2048u + j * box_bytes, &tmv, bar, hf * 64, 0, h,
+                        phys);
+          }
+        }
+      }
+    }
+  };
+
+  for (int s = 0; s < stages && pf < we; ++s) {
+    issue(s);
+    advance(pc);
+    ++pf;
+  }
+
+  // ---- consumer ----
+  const int qrow0 = lane >> 2;  // rows qrow0 and qrow0 + 8 of the m16 tile
+  const int quad = lane & 3;
+  const int slot_floats = p.slot_rows * (2 + D);
+
+  Cursor cc = start;
+  long long cf = ws;
+  int slot = 0;
+  uint32_t phase = 0;
+
+  uint32_t qa[KSTEPS][4];
+  float o_acc[NDT][4];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  int lim0 = 0, lim1 = 0;  // last attendable token of rows qrow0 / qrow0 + 8
+  bool piece_first = true, piece_from_row_start = false;
+
+  while (cf < we) {
+    const int b = cc.b;
+    const int h = cc.r / p.NMG;
+    const int mg = cc.r - h * p.NMG;
+    const int L = s_lens[b];
+
+    if (cc.u == 0 || cf == ws) {
+      // Begin a piece: load the packed query tile of (b, h, m-group) as A fragments.
+      piece_first = (cf == ws);
+      piece_from_row_start = (cc.u == 0);
+      const int qr0 = mg * 16 + qrow0;
+      const int qr1 = qr0 + 8;
+      const T* qp0 = nullptr;
+      const T* qp1 = nullptr;
+      lim0 = L - 1;
+      lim1 = L - 1;
+      if (qr0 < p.GQ) {
+        const int g = qr0 / p.q_len, t = qr0 - (qr0 / p.q_len) * p.q_len;
+        qp0 = static_cast<const T*>(p.q) + (long long)b * p.q_sb +
+              (long long)(h * p.G + g) * p.q_sh + (long long)t * p.q_st;
+        lim0 = L - p.q_len + t;
+      }
+      if (qr1 < p.GQ) {
+        const int g = qr1 / p.q_len, t = qr1 - (qr1 / p.q_len) * p.q_len;
+        qp1 = static_cast<const T*>(p.q) + (long long)b * p.q_sb +
+              (long long)(h * p.G + g) * p.q_sh + (long long)t * p.q_st;
+        lim1 = L - p.q_len + t;
+      }
+#pragma unroll
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+        const int d = ks * 16 + 2 * quad;
+        qa[ks][0] = qp0 ? __ldg(reinterpret_cast<const unsigned int*>(qp0 + d)) : 0u;
+        qa[ks][1] = qp1 ? __ldg(reinterpret_cast<const unsigned int*>(qp1 + d)) : 0u;
+        qa[ks][2] = qp0 ? __ldg(reinterpret_cast<const unsigned int*>(qp0 + d + 8)) : 0u;
+        qa[ks][3] = qp1 ? __ldg(reinterpret_cast<const unsigned int*>(qp1 + d + 8)) : 0u;
+      }
+#pragma unroll
+      for (int nd = 0; nd < NDT; ++nd) {
+        o_acc[nd][0] = o_acc[nd][1] = o_acc[nd][2] = o_acc[nd][3] = 0.f;
+      }
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
+    }
+
+    // ---- wait for this unit's K/V tiles ----
+    const uint32_t bar = my_bars + (uint32_t)slot * 8u;
+    if (!mbar_wait_bounded(bar, (phase >> slot) & 1u)) {
+      if (lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
+      // Drain this warp's copies still in flight (bounded), then leave.
+      int s = slot;
+      for (long long k = cf; k < pf; ++k) {
+        mbar_wait_bounded(my_bars + (uint32_t)s * 8u, (phase >> s) & 1u);
+        s = (s + 1 == stages) ? 0 : s + 1;
+      }
+      return;
+    }
+    phase ^= (1u << slot);
+
+    const uint32_t kbase = my_ring + (uint32_t)slot * STAGE_BYTES;
+    const uint32_t vbase = kbase + TILE_BYTES;
+
+    // ---- S = Q K^T (16 query rows x 16 tokens), fp32 accumulate ----
+    float s_acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      const int tok = ((lane >> 4) << 3) | (lane & 7);
+#pragma unroll
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+        const int chunk = 2 * ks + ((lane >> 3) & 1);
+        const uint32_t addr = kbase + (uint32_t)(chunk >> 3) * 2048u + (uint32_t)tok * 128u +
+                              ((uint32_t)((chunk & 7) ^ (tok & 7)) << 4);
+        uint32_t k0, k1, k2, k3;
+        ldsm_x4(addr, k0, k1, k2, k3);
+        Mma16816<T>::run(s_acc[0], qa[ks], k0, k1);
+        Mma16816<T>::run(s_acc[1], qa[ks], k2, k3);
+      }
+    }
+
+    // ---- scale, mask, online softmax ----
+    const int tok_base = cc.u * kUnitTokens;
+    float x[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[n][i] = s_acc[n][i] * p.scale_log2;
+    if (tok_base + kUnitTokens - 1 > L - p.q_len) {
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int tok = tok_base + n * 8 + 2 * quad + (i & 1);
+          const int lim = (i < 2) ? lim0 : lim1;
+          if (tok > lim) x[n][i] = -INFINITY;
+        }
+    }
+    float mx0 = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
+    float mx1 = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0);
+    const float mn1 = fmaxf(m1, mx1);
+    const float base0 = (mn0 == -INFINITY) ? 0.f : mn0;
+    const float base1 = (mn1 == -INFINITY) ? 0.f : mn1;
+    const float alpha0 = ex2(m0 - base0);
+    const float alpha1 = ex2(m1 - base1);
+    float pr[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      pr[n][0] = ex2(x[n][0] - base0);
+      pr[n][1] = ex2(x[n][1] - base0);
+      pr[n][2] = ex2(x[n][2] - base1);
+      pr[n][3] = ex2(x[n][3] - base1);
+    }
+    l0 = l0 * alpha0 + (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+    l1 = l1 * alpha1 + (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int nd = 0; nd < NDT; ++nd) {
+      o_acc[nd][0] *= alpha0;
+      o_acc[nd][1] *= alpha0;
+      o_acc[nd][2] *= alpha1;
+      o_acc[nd][3] *= alpha1;
+    }
+    uint32_t pa[4];
+    pa[0] = pack2<T>(pr[0][0], pr[0][1]);
+    pa[1] = pack2<T>(pr[0][2], pr[0][3]);
+    pa[2] = pack2<T>(pr[1][0], pr[1][1]);
+    pa[3] = pack2<T>(pr[1][2], pr[1][3]);
+
+    // ---- O += P V ----
+    {
+      // Tokens at or past L hold whatever the cache had there; zero them so a
+      // non-finite stale value cannot turn 0 * v into NaN.
+      uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
+      if (tok_base + kUnitTokens > L) {
+        const int t0 = tok_base + 2 * quad;
+        vm0 = (t0 < L ? 0x0000ffffu : 0u) | (t0 + 1 < L ? 0xffff0000u : 0u);
+        vm1 = (t0 + 8 < L ? 0x0000ffffu : 0u) | (t0 + 9 < L ? 0xffff0000u : 0u);
+      }
+      const int tok = (((lane >> 3) & 1) << 3) | (lane & 7);
+#pragma unroll
+      for (int nd = 0; nd < NDT; nd += 2) {
+        const int chunk = nd + (lane >> 4);
+        const uint32_t addr = vbase + (uint32_t)(chunk >> 3) * 2048u + (uint32_t)tok * 128u +
+                              ((uint32_t)((chunk & 7) ^ (tok & 7)) << 4);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_trans(addr, v0, v1, v2, v3);
+        v0 &= vm0;
+        v1 &= vm1;
+        v2 &= vm0;
+        v3 &= vm1;
+        Mma16816<T>::run(o_acc[nd], pa, v0, v1);
+        Mma16816<T>::run(o_acc[nd + 1], pa, v2, v3);
+      }
+    }
+
+    // ---- refill this slot with the unit `stages` ahead ----
+    __syncwarp();
+    if (pf < we) {
+      fence_proxy_async_smem();
+      issue(slot);
+      advance(pc);
+      ++pf;
+    }
+
+    // ---- end of a piece: write the output or a partial and merge ----
+    const bool row_end = (cc.u + 1 == cc.n);
+    if (row_end || cf + 1 == we) {
+      float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+      float lt1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+      lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
+      lt1 += __shfl_xor_sync(0xffffffffu, lt1, 2);
+      const int rows_here = min(16, p.GQ - mg * 16);
+      const bool r0_ok = qrow0 < rows_here;
+      const bool r1_ok = qrow0 + 8 < rows_here;
+      if (row_end && piece_from_row_start) {
+        // The whole row is in this piece: normalise and store.
+        const float inv0 = lt0 > 0.f ? 1.f / lt0 : 0.f;
+        const float inv1 = lt1 > 0.f ? 1.f / lt1 : 0.f;
+        T* op0 = nullptr;
+        T* op1 = nullptr;
+        if (r0_ok) {
+          const int qr = mg * 16 + qrow0;
+          const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+          op0 = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
+                (long long)t * p.o_st;
+        }
+        if (r1_ok) {
+          const int qr = mg * 16 + qrow0 + 8;
+          const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+          op1 = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
+                (long long)t * p.o_st;
+        }
+#pragma unroll
+        for (int nd = 0; nd < NDT; ++nd) {
+          const int d = nd * 8 + 2 * quad;
+          if (op0)
+            *reinterpret_cast<uint32_t*>(op0 + d) =
+                pack2<T>(o_acc[nd][0] * inv0, o_acc[nd][1] * inv0);
+          if (op1)
+            *reinterpret_cast<uint32_t*>(op1 + d) =
+                pack2<T>(o_acc[nd][2] * inv1, o_acc[nd][3] * inv1);
+        }
+      } else {
+        // Partial: (m, l, acc) to this warp's slot, then count the arrival.
+        const int slot_idx = 2 * gw + (piece_first ? 0 : 1);
+        float* sl = p.partials + (long long)slot_idx * slot_floats;
+        if (quad == 0) {
+          if (r0_ok) {
+            sl[qrow0] = m0;
+            sl[p.slot_rows + qrow0] = lt0;
+          }
+          if (r1_ok) {
+            sl[qrow0 + 8] = m1;
+            sl[p.slot_rows + qrow0 + 8] = lt1;
+          }
+        }
+        float* so = sl + 2 * p.slot_rows;
+#pragma unroll
+        for (int nd = 0; nd < NDT; ++nd) {
+          const int d = nd * 8 + 2 * quad;
+          if (r0_ok)
+            *reinterpret_cast<float2*>(so + qrow0 * D + d) = make_float2(o_acc[nd][0], o_acc[nd][1]);
+          if (r1_ok)
+            *reinterpret_cast<float2*>(so + (qrow0 + 8) * D + d) =
+                make_float2(o_acc[nd][2], o_acc[nd][3]);
+        }
+        __threadfence();
+        __syncwarp();
+        const long long row_start = cf - cc.u;
+        const long long row_stop = row_start + cc.n;  // exclusive
+        const int gw1 = (int)(((row_start + 1) * nw_eff - 1) / W);
+        const int gw2 = (int)((row_stop * nw_eff - 1) / W);
+        const int npieces = gw2 - gw1 + 1;
+        const int row_id = b * rows_per_b + cc.r;
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&p.counters[row_id], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == npieces - 1) {
+          // Last arrival: log-sum-exp merge of all pieces of this row.
+          __threadfence();
+          const bool gw1_first = (W * gw1 / nw_eff) == row_start;
+          for (int r = 0; r < rows_here; ++r) {
+            float M = -INFINITY;
+            for (int g2 = gw1; g2 <= gw2; ++g2) {
+              const int si = (g2 == gw1 && !gw1_first) ? 2 * g2 + 1 : 2 * g2;
+              M = fmaxf(M, __ldcg(p.partials + (long long)si * slot_floats + r));
+            }
+            const float Mb = (M == -INFINITY) ? 0.f : M;
+            float lsum = 0.f;
+            float acc[DPL];
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) acc[k] = 0.f;
+            for (int g2 = gw1; g2 <= gw2; ++g2) {
+              const int si = (g2 == gw1 && !gw1_first) ? 2 * g2 + 1 : 2 * g2;
+              const float* ps = p.partials + (long long)si * slot_floats;
+              const float w = ex2(__ldcg(ps + r) - Mb);
+              lsum += w * __ldcg(ps + p.slot_rows + r);
+              const float* po = ps + 2 * p.slot_rows + r * D;
+#pragma unroll
+              for (int k = 0; k < DPL; ++k) acc[k] += w * __ldcg(po + lane + 32 * k);
+            }
+            const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+            const int qr = mg * 16 + r;
+            const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+            T* op = static_cast<T*>(p.out) + (long long)b * p.o_sb +
+                    (long long)(h * p.G + g) * p.o_sh + (long long)t * p.o_st;
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) op[lane + 32 * k] = from_float<T>(acc[k] * inv);
+          }
+          if (lane == 0) atomicExch(&p.counters[row_id], 0);
+        }
+      }
+    }
+
+    advance(cc);
+    ++cf;
+    slot = (slot + 1 == stages) ? 0 : slot + 1;
+  }
+}
+
+size_t decode_mma_smem_bytes(int D, int B, int stages) {
+  const size_t stage_bytes = 2u * 16u * (size_t)D * 2u;
+  return 1024 + (size_t)kDecodeWarps * stages * stage_bytes + (size_t)kDecodeWarps * stages * 8 +
+         (size_t)(2 * B + 1) * 4;
+}
+
+template <typename T, int D>
+static cudaError_t launch_mma_impl(const DecodeParams& p, const CUtensorMap& tmk,
+                                   const CUtensorMap& tmv, int grid, size_t smem, bool pdl,
+                                   cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kDecodeWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<T, D>, tmk, tmv, p);
+}
+
+cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                              int dtype, int grid, size_t smem, bool pdl, cudaStream_t stream) {
+  if (dtype == PA_DTYPE_BFLOAT16) {
+    if (p.D == 128) return launch_mma_impl<__nv_bfloat16, 128>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 64) return launch_mma_impl<__nv_bfloat16, 64>(p, tmk, tmv, grid, smem, pdl, stream);
+  } else if (dtype == PA_DTYPE_FLOAT16) {
+    if (p.D == 128) return launch_mma_impl<__half, 128>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 64) return launch_mma_impl<__half, 64>(p, tmk, tmv, grid, smem, pdl, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t decode_mma_prepare(int dtype, int D, size_t smem) {
+  const void* fn = nullptr;
+  if (dtype == PA_DTYPE_BFLOAT16)
+    fn = D == 128 ? (const void*)decode_mma_kernel<__nv_bfloat16, 128>
+                  : (const void*)decode_mma_kernel<__nv_bfloat16, 64>;
+  else
+    fn = D == 128 ? (const void*)decode_mma_kernel<__half, 128> : (const void*)decode_mma_kernel<__half, 64>;
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+}  // namespace pa

@@ -1,0 +1,86 @@
+// pa_internal.h — host-side plumbing shared by the kernel translation units and
+// the C ABI (pa_capi.cu).  Not part of the public interface.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/paged_attention_b200.h"
+
+namespace pa {
+
+// Warps per CTA of the tensor-core decode kernel.  Each warp is a self-fed
+// engine with its own ring of shared-memory stages.
+constexpr int kDecodeWarps = 8;
+// Minimum number of 16-token units a warp's share of the flat work list holds
+// before the kernel stops splitting the work further.
+constexpr int kMinUnitsPerWarp = 8;
+// Layout of the workspace: status word, then merge counters, then partial slots.
+constexpr size_t kWsHeaderBytes = 256;
+
+// Kernel-side description of one decode call (passed by value).
+struct DecodeParams {
+  const void* q;
+  int64_t q_sb, q_sh, q_st;
+  const void* k_cache;  // used by the CUDA-core kernel (the tensor-core kernel uses TMA maps)
+  const void* v_cache;
+  int64_t k_sblk, k_sh, k_st;
+  int64_t v_sblk, v_sh, v_st;
+  int64_t num_blocks;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int32_t max_blocks;
+  const int32_t* context_lens;
+  int32_t len_offset;
+  void* out;
+  int64_t o_sb, o_sh, o_st;
+  int32_t B, q_len, Hq, Hkv, G, GQ, NMG, bs, D;
+  float scale;       // softmax scale
+  float scale_log2;  // scale * log2(e)
+  uint32_t* status;  // device error word
+  int32_t* counters; // [B * Hkv * NMG] merge arrival counters (kept at zero between calls)
+  float* partials;   // [2 * nw_total] slots of (m, l, O) partial states
+  int32_t slot_rows; // rows stored per partial slot
+  int32_t nw_total;  // warps in the grid
+  int32_t stages;    // shared-memory ring depth per warp
+};
+
+struct AppendParams {
+  const void* key;
+  int64_t k_sb, k_sh, k_st;
+  const void* value;
+  int64_t v_sb, v_sh, v_st;
+  void* k_cache;
+  int64_t kc_sblk, kc_sh, kc_st;
+  void* v_cache;
+  int64_t vc_sblk, vc_sh, vc_st;
+  int64_t num_blocks;
+  const int64_t* slot_mapping;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int32_t max_blocks;
+  const void* positions;
+  int32_t positions_is_int64;
+  int32_t position_offset;
+  int32_t B, q_len, Hkv, D, bs, elem_bytes;
+  uint32_t* error_flags;
+};
+
+// Workspace layout helpers (bytes).
+size_t ws_counter_bytes(int B, int Hkv, int NMG);
+size_t ws_partial_bytes(int nw_total, int slot_rows, int D);
+
+// Launchers (return cudaError_t of the launch).
+cudaError_t launch_kv_append(const AppendParams& p, cudaStream_t stream);
+cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                              int dtype, int grid, size_t smem, bool pdl, cudaStream_t stream);
+cudaError_t launch_decode_f32(const DecodeParams& p, bool pdl, cudaStream_t stream);
+
+// Shared-memory bytes of the tensor-core kernel for given stage count.
+size_t decode_mma_smem_bytes(int D, int B, int stages);
+// Opt a kernel instantiation into large dynamic shared memory (once per device).
+cudaError_t decode_mma_prepare(int dtype, int D, size_t smem);
+
+}  // namespace pa

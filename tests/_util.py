@@ -1,0 +1,43 @@
+"""Helpers shared by the GPU parity tests: run the oracle on a subset of rows."""
+
+from __future__ import annotations
+
+import torch
+
+from oracle import oracle
+
+TOL = {torch.float32: 1e-5, torch.float16: 2e-3, torch.bfloat16: 2e-3}
+
+
+def compact_rows(query, key_cache, value_cache, block_tables, context_lens, q_len, rows):
+    """CPU copies of just what ``rows`` attend: their query rows, their blocks
+    gathered into a small pool, and block tables renumbered into it."""
+    rows_t = torch.as_tensor(rows, dtype=torch.long, device=block_tables.device)
+    bs = key_cache.shape[2]
+    lens = context_lens[rows_t].to(torch.int64) + q_len
+    nblk = (lens + bs - 1) // bs
+    maxb = int(nblk.max().item())
+    tables = block_tables[rows_t, :maxb].to(torch.int64)
+    ids = []
+    new_tables = torch.zeros(len(rows), maxb, dtype=torch.int32)
+    cursor = 0
+    for i in range(len(rows)):
+        n = int(nblk[i])
+        ids.append(tables[i, :n])
+        new_tables[i, :n] = torch.arange(cursor, cursor + n, dtype=torch.int32)
+        cursor += n
+    ids = torch.cat(ids)
+    kc = key_cache[ids].cpu()
+    vc = value_cache[ids].cpu()
+    return query[rows_t].cpu(), kc, vc, new_tables, context_lens[rows_t].cpu()
+
+
+def oracle_rows(query, key_cache, value_cache, block_tables, context_lens, scale, q_len, rows):
+    q, kc, vc, bt, cl = compact_rows(query, key_cache, value_cache, block_tables, context_lens, q_len, rows)
+    return oracle.paged_decode(q, kc, vc, bt, cl, scale, len_offset=q_len)
+
+
+def max_err(out: torch.Tensor, ref_f32: torch.Tensor) -> float:
+    """Max abs difference with the fp32 oracle rounded to the output dtype (the
+    reference rounds its fp32 result the same way, paged_attention_triton.py:703)."""
+    return (out.float().cpu() - ref_f32.to(out.dtype).float().cpu()).abs().max().item()

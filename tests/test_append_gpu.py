@@ -1,0 +1,113 @@
+"""KV append on the GPU: bit-exact against the reference's write_tokens_batch
+(golden vectors) and the oracle's slot-mapping scatter."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import load_golden
+from llm_serving_runtime_b200 import kv_append, read_device_errors
+from llm_serving_runtime_b200.kv_block_pool import GpuKVBlockPool
+from llm_serving_runtime_b200.workloads import make_workload
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _bits(t):
+    return t.cpu().contiguous().view(torch.int16 if t.element_size() == 2 else torch.int32)
+
+
+@pytest.mark.parametrize("case", ["append_fp16", "append_bf16"])
+@pytest.mark.parametrize("pos_dtype", [torch.int64, torch.int32])
+def test_write_tokens_batch_matches_reference_bits(case, pos_dtype):
+    data, meta = load_golden(case)
+    layer = meta["layer_idx"]
+    kp = data["k_pool_before"].to(DEV)
+    vp = data["v_pool_before"].to(DEV)
+    kv_append(data["key_states"].to(DEV), data["value_states"].to(DEV), kp[:, layer], vp[:, layer],
+              block_tables=data["block_tables"].to(DEV), positions=data["start_positions"].to(pos_dtype).to(DEV),
+              validate=True)
+    assert torch.equal(_bits(kp), _bits(data["k_pool_after"]))
+    assert torch.equal(_bits(vp), _bits(data["v_pool_after"]))
+
+
+@pytest.mark.parametrize("case", ["append_fp16", "append_bf16"])
+def test_pool_mirror_write_tokens_batch(case):
+    data, meta = load_golden(case)
+    kp0 = data["k_pool_before"]
+    nb, L, Hkv, bs, D = kp0.shape
+    pool = GpuKVBlockPool(num_blocks=nb, block_size_tokens=bs, num_layers=L, num_kv_heads=Hkv, head_dim=D,
+                          dtype=kp0.dtype, device=DEV)
+    pool._grow_pools(nb)
+    pool._k_pool.copy_(kp0.to(DEV))
+    pool._v_pool.copy_(data["v_pool_before"].to(DEV))
+    pool.write_tokens_batch(meta["layer_idx"], data["block_tables"], data["start_positions"],
+                            data["key_states"].to(DEV), data["value_states"].to(DEV))
+    assert torch.equal(_bits(pool._k_pool), _bits(data["k_pool_after"]))
+    assert torch.equal(_bits(pool._v_pool), _bits(data["v_pool_after"]))
+    with pytest.raises(IndexError, match="underrun"):
+        pool.write_tokens_batch(0, data["block_tables"], torch.tensor([2, 7, 14]),
+                                data["key_states"].to(DEV), data["value_states"].to(DEV))
+
+
+def test_roundtrip_reference_test():
+    # tests/test_paged_kv_kernel.py:11-28 on the GPU pool
+    data, _ = load_golden("roundtrip_fp32")
+    pool = GpuKVBlockPool(num_blocks=4, block_size_tokens=2, num_layers=1, num_kv_heads=2, head_dim=4,
+                          dtype=torch.float32, device=DEV)
+    pool.write_tokens(0, [0, 1], 0, data["key_states"].to(DEV), data["value_states"].to(DEV))
+    keys, values = pool.gather_layer(0, [0, 1], 2)
+    assert keys.shape == (1, 2, 2, 4)
+    assert torch.equal(keys.cpu(), data["keys"]) and torch.equal(values.cpu(), data["values"])
+
+
+@pytest.mark.parametrize("name", ["cfg1-fp32-small", "cfg2-qwen2-0.5b", "cfg4-prefix-verify"])
+def test_slot_mapping_append_bit_exact_vs_oracle(name):
+    w = make_workload(name, device="cpu")
+    kc, vc = w.key_cache.clone(), w.value_cache.clone()
+    oracle.kv_append(w.new_key, w.new_value, kc, vc, w.slot_mapping)
+    wd = w.to(DEV)
+    kv_append(wd.new_key, wd.new_value, wd.key_cache, wd.value_cache, wd.slot_mapping, validate=True)
+    assert torch.equal(_bits(wd.key_cache), _bits(kc))
+    assert torch.equal(_bits(wd.value_cache), _bits(vc))
+
+
+def test_derived_slots_equal_explicit_slots():
+    w = make_workload("cfg4-prefix-verify", device=DEV)
+    k1, v1 = w.key_cache.clone(), w.value_cache.clone()
+    k2, v2 = w.key_cache.clone(), w.value_cache.clone()
+    kv_append(w.new_key, w.new_value, k1, v1, w.slot_mapping)
+    kv_append(w.new_key, w.new_value, k2, v2, block_tables=w.block_tables, positions=w.context_lens)
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)
+
+
+def test_padding_slots_are_skipped_and_bad_slots_flagged():
+    w = make_workload("cfg2-qwen2-0.5b", device=DEV)
+    kc, vc = w.key_cache.clone(), w.value_cache.clone()
+    slots = w.slot_mapping.clone()
+    slots[3] = -1
+    kv_append(w.new_key, w.new_value, kc, vc, slots, validate=True)
+    # row 3's slot untouched
+    s = int(w.slot_mapping[3])
+    bs = kc.shape[2]
+    assert torch.equal(kc[s // bs, :, s % bs], w.key_cache[s // bs, :, s % bs])
+    assert not torch.equal(kc[s // bs, :, s % bs], w.new_key[3, :, 0])
+    read_device_errors(DEV)
+    slots[5] = kc.shape[0] * bs + 3  # outside the pool: skipped and flagged
+    with pytest.raises(IndexError, match="slot"):
+        kv_append(w.new_key, w.new_value, kc, vc, slots, validate=True)
+
+
+def test_non_contiguous_new_rows():
+    # HF gives key_states as [B, q, H, D] transposed to [B, H, q, D].
+    w = make_workload("cfg4-prefix-verify", device=DEV)
+    k_hf = w.new_key.transpose(1, 2).contiguous().transpose(1, 2)
+    v_hf = w.new_value.transpose(1, 2).contiguous().transpose(1, 2)
+    k1, v1 = w.key_cache.clone(), w.value_cache.clone()
+    kv_append(k_hf, v_hf, k1, v1, w.slot_mapping)
+    k2, v2 = w.key_cache.clone(), w.value_cache.clone()
+    kv_append(w.new_key, w.new_value, k2, v2, w.slot_mapping)
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)

@@ -1,0 +1,281 @@
+"""Parity of the sm_100a decode kernels with the reference (golden vectors) and
+with the oracle, through the C ABI (ctypes -> libpa_b200.so).
+
+Tolerance (north star): max-abs error <= 2e-3 for fp16/bf16 and <= 1e-5 for
+fp32, against the fp32 oracle rounded to the output dtype.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from _util import TOL, max_err, oracle_rows
+from conftest import decode_cases, load_golden
+from llm_serving_runtime_b200 import paged_attention_decode, read_device_errors
+from llm_serving_runtime_b200.workloads import make_workload
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _run_golden(case):
+    data, meta = load_golden(case)
+    include = meta["lens_include_query"]
+    lens = data["seq_lens"] if include else data["context_lens"]
+    out = paged_attention_decode(
+        data["query"].to(DEV), data["key_cache"].to(DEV), data["value_cache"].to(DEV),
+        data["block_tables"].to(DEV), lens.to(DEV), meta["scale"], context_lens_include_new=include,
+        validate=True,
+    )
+    return data, meta, out
+
+
+@pytest.mark.parametrize("case", [c for c in decode_cases() if c != "cfg1_fp32"])
+def test_golden_decode(case):
+    data, meta, out = _run_golden(case)
+    expected = data.get("expected_torch", data.get("expected_eager"))
+    tol = TOL[expected.dtype]
+    err = (out.float().cpu() - expected.float()).abs().max().item()
+    # expected is the reference's fp32 result rounded to the dtype; allow one
+    # rounding step of the dtype on top of the north-star tolerance for 16-bit.
+    assert err <= tol, f"{case}: max abs err {err} > {tol}"
+
+
+def test_golden_reference_own_tolerance_vs_sdpa():
+    # the reference's parity bar, tests/test_paged_attention_kernel_parity.py:79
+    for case in ("fp32_short", "fp32_longer", "fp16_128", "fp16_long_split"):
+        data, meta, out = _run_golden(case)
+        err = (out.float().cpu() - data["expected_sdpa"].float()).abs().max().item()
+        assert err < 1e-2, (case, err)
+
+
+def test_config1_append_and_decode_bit_exact_append():
+    import hashlib
+
+    data, meta = load_golden("cfg1_fp32")
+    w = make_workload("cfg1-fp32-small", device="cpu").to(DEV)
+    kc, vc = w.key_cache.clone(), w.value_cache.clone()
+    out = paged_attention_decode(w.query, kc, vc, w.block_tables, w.context_lens, w.scale,
+                                 w.slot_mapping, w.new_key, w.new_value, validate=True)
+    sha = lambda t: hashlib.sha256(t.cpu().contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+    assert sha(kc) == meta["k_cache_after_sha256"]
+    assert sha(vc) == meta["v_cache_after_sha256"]
+    assert max_err(out, data["expected_torch"]) <= TOL[torch.float32]
+
+
+def _config_parity(name, rows_sample=None, seed_rows=0):
+    w = make_workload(name, device=DEV)
+    out = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens,
+                                 w.scale, w.slot_mapping, w.new_key, w.new_value, validate=True)
+    torch.cuda.synchronize()
+    B = w.batch
+    if rows_sample is None:
+        rows = list(range(B))
+    else:
+        g = torch.Generator().manual_seed(seed_rows)
+        rows = sorted(torch.randperm(B, generator=g)[:rows_sample].tolist())
+        # always include the longest and the shortest row
+        L = w.context_lens.cpu()
+        rows = sorted(set(rows) | {int(L.argmax()), int(L.argmin())})
+    ref = oracle_rows(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                      w.q_len, rows)
+    err = max_err(out[rows], ref)
+    assert err <= TOL[w.spec.dtype], f"{name}: max abs err {err}"
+    return w, out
+
+
+def test_config2_qwen2_full_batch():
+    _config_parity("cfg2-qwen2-0.5b")
+
+
+def test_config3_llama3_8b_sampled_rows():
+    _config_parity("cfg3-llama3-8b", rows_sample=40)
+
+
+def test_config4_prefix_shared_verify_q4():
+    _config_parity("cfg4-prefix-verify", rows_sample=24)
+
+
+def test_config5_llama3_70b_sampled_rows():
+    w, out = _config_parity("cfg5-llama3-70b", rows_sample=6)
+    del w, out
+    torch.cuda.empty_cache()
+
+
+def _synthetic(B, Hq, Hkv, D, bs, dtype, lens, q_len=1, seed=0, pool_extra=5, scale_v=0.5):
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.as_tensor(lens, dtype=torch.int64)
+    att = lens + q_len
+    nblk = (att + bs - 1) // bs
+    maxb = max(1, int(nblk.max()))
+    nb = int(nblk.sum()) + pool_extra
+    perm = torch.randperm(nb, generator=g)
+    bt = torch.zeros(B, maxb, dtype=torch.int32)
+    c = 0
+    for i in range(B):
+        n = int(nblk[i])
+        bt[i, :n] = perm[c:c + n].to(torch.int32)
+        c += n
+    kc = (torch.randn(nb, Hkv, bs, D, generator=g) * scale_v).to(dtype)
+    vc = (torch.randn(nb, Hkv, bs, D, generator=g) * scale_v).to(dtype)
+    q = (torch.randn(B, Hq, q_len, D, generator=g) * scale_v).to(dtype)
+    return q, kc, vc, bt, lens.to(torch.int32)
+
+
+EDGE = [
+    # (B, Hq, Hkv, D, bs, dtype, lens, q_len)
+    (6, 8, 2, 128, 16, torch.bfloat16, [0, 14, 15, 16, 31, 32], 1),
+    (5, 32, 8, 128, 16, torch.bfloat16, [1, 100, 4095, 8191, 3], 1),
+    (4, 14, 2, 64, 16, torch.float16, [127, 128, 129, 2047], 1),
+    (3, 8, 8, 128, 16, torch.bfloat16, [5, 77, 300], 1),          # G = 1 (MHA)
+    (3, 16, 1, 64, 16, torch.float16, [40, 41, 500], 1),          # G = 16 (one full m-tile)
+    (3, 64, 8, 128, 16, torch.bfloat16, [2048, 3000, 9], 1),      # G = 8
+    (4, 32, 8, 128, 16, torch.bfloat16, [0, 12, 13, 1000], 4),    # q_len 4, causal
+    (3, 64, 8, 128, 16, torch.bfloat16, [20, 33, 700], 4),        # G*q = 32: two row groups
+    (3, 14, 2, 64, 16, torch.float16, [1, 2, 300], 2),            # G*q = 14
+    (4, 8, 2, 128, 8, torch.bfloat16, [0, 7, 8, 250], 1),         # block size 8
+    (4, 8, 2, 64, 32, torch.float16, [0, 31, 32, 1000], 1),       # block size 32
+    (3, 8, 2, 128, 64, torch.bfloat16, [63, 64, 513], 2),         # block size 64
+    (4, 8, 2, 64, 4, torch.float32, [0, 3, 4, 77], 1),            # fp32, block size 4
+    (3, 8, 2, 128, 16, torch.float32, [10, 31, 300], 4),          # fp32, causal
+    (2, 4, 2, 32, 16, torch.float32, [5, 64], 1),                 # fp32, head_dim 32
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,bs,dtype,lens,q_len", EDGE)
+def test_edge_shapes_vs_oracle(B, Hq, Hkv, D, bs, dtype, lens, q_len):
+    q, kc, vc, bt, cl = _synthetic(B, Hq, Hkv, D, bs, dtype, lens, q_len, seed=B * 7 + D)
+    scale = D ** -0.5
+    out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), scale, validate=True)
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, scale)
+    assert max_err(out, ref) <= TOL[dtype]
+
+
+def test_one_long_sequence_split_over_the_whole_grid():
+    # B = 1, 64k tokens: every warp of the grid takes a slice of the one row,
+    # so the log-sum-exp merge combines hundreds of partials.
+    q, kc, vc, bt, cl = _synthetic(1, 32, 8, 128, 16, torch.bfloat16, [65535], seed=3)
+    out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), 128 ** -0.5,
+                                 validate=True)
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, 128 ** -0.5)
+    assert max_err(out, ref) <= TOL[torch.bfloat16]
+
+
+def test_many_short_sequences_and_large_batch():
+    lens = torch.randint(0, 64, (3000,), generator=torch.Generator().manual_seed(1)).tolist()
+    q, kc, vc, bt, cl = _synthetic(3000, 8, 2, 128, 16, torch.bfloat16, lens, seed=4)
+    out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), 128 ** -0.5,
+                                 validate=True)
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, 128 ** -0.5)
+    assert max_err(out, ref) <= TOL[torch.bfloat16]
+
+
+def test_strided_pool_layer_view_and_transposed_query():
+    # GpuKVBlockPool layout [num_blocks, layers, Hkv, bs, D]; layer 1 of 3; query
+    # as HF produces it ([B, q, H, D] transposed to [B, H, q, D]).
+    B, Hq, Hkv, D, bs = 4, 32, 8, 128, 16
+    q, kc, vc, bt, cl = _synthetic(B, Hq, Hkv, D, bs, torch.bfloat16, [17, 250, 16, 1], seed=9)
+    nb = kc.shape[0]
+    kpool = torch.randn(nb, 3, Hkv, bs, D).to(torch.bfloat16)
+    vpool = torch.randn(nb, 3, Hkv, bs, D).to(torch.bfloat16)
+    kpool[:, 1] = kc
+    vpool[:, 1] = vc
+    kpool, vpool = kpool.to(DEV), vpool.to(DEV)
+    q_hf = q.transpose(1, 2).contiguous().to(DEV).transpose(1, 2)
+    assert not q_hf.is_contiguous()
+    out = paged_attention_decode(q_hf, kpool[:, 1], vpool[:, 1], bt.to(DEV), cl.to(DEV), D ** -0.5,
+                                 validate=True)
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, D ** -0.5)
+    assert max_err(out, ref) <= TOL[torch.bfloat16]
+
+
+def test_non_finite_values_past_the_sequence_end_do_not_leak():
+    # Slots past L in the last block hold NaN/Inf (an uninitialised pool): the
+    # output must not see them (the reference masks its loads, :208-226).
+    B, Hq, Hkv, D, bs = 3, 8, 2, 128, 16
+    q, kc, vc, bt, cl = _synthetic(B, Hq, Hkv, D, bs, torch.bfloat16, [4, 20, 33], seed=5)
+    kc_d, vc_d = kc.to(DEV), vc.to(DEV)
+    for b in range(B):
+        L = int(cl[b]) + 1
+        last = int(bt[b, (L - 1) // bs])
+        off = L % bs
+        if off:
+            kc_d[last, :, off:] = float("nan")
+            vc_d[last, :, off:] = float("inf")
+    out = paged_attention_decode(q.to(DEV), kc_d, vc_d, bt.to(DEV), cl.to(DEV), D ** -0.5, validate=True)
+    assert torch.isfinite(out.float()).all()
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, D ** -0.5)
+    assert max_err(out, ref) <= TOL[torch.bfloat16]
+
+
+def test_deterministic_bitwise():
+    q, kc, vc, bt, cl = _synthetic(64, 32, 8, 128, 16, torch.bfloat16,
+                                   torch.randint(1, 3000, (64,), generator=torch.Generator().manual_seed(2)).tolist())
+    args = [t.to(DEV) for t in (q, kc, vc, bt, cl)]
+    a = paged_attention_decode(*args, 128 ** -0.5)
+    b = paged_attention_decode(*args, 128 ** -0.5)
+    assert torch.equal(a, b)
+
+
+def test_rows_with_nothing_to_attend_are_zero():
+    q, kc, vc, bt, cl = _synthetic(3, 8, 2, 128, 16, torch.bfloat16, [0, 40, 0], seed=6)
+    # context_lens_include_new=True with 0 -> nothing to attend
+    out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV),
+                                 torch.tensor([0, 41, 0], dtype=torch.int32, device=DEV), 128 ** -0.5,
+                                 context_lens_include_new=True)
+    assert torch.count_nonzero(out[0]) == 0 and torch.count_nonzero(out[2]) == 0
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, 128 ** -0.5)
+    assert max_err(out[1:2], ref[1:2]) <= TOL[torch.bfloat16]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_out_of_range_block_id_is_flagged_not_faulted(dtype):
+    q, kc, vc, bt, cl = _synthetic(2, 8, 2, 64, 16, dtype, [40, 40], seed=8)
+    read_device_errors(DEV)  # clear
+    bt[1, 1] = kc.shape[0] + 5  # outside the pool: TMA zero-fills / the fp32 kernel skips
+    with pytest.raises(IndexError, match="out of range"):
+        paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), 0.125, validate=True)
+    assert read_device_errors(DEV) == 0  # cleared by the failing call
+
+
+def test_table_underrun_is_flagged():
+    q, kc, vc, bt, cl = _synthetic(2, 8, 2, 64, 16, torch.float16, [40, 40], seed=8)
+    cl[0] = 10_000  # needs far more blocks than the table holds
+    with pytest.raises(IndexError, match="underrun"):
+        paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), 0.125, validate=True)
+
+
+def test_shape_errors_are_value_errors():
+    q, kc, vc, bt, cl = _synthetic(2, 8, 2, 64, 16, torch.float16, [4, 4], seed=1)
+    q, kc, vc, bt, cl = (t.to(DEV) for t in (q, kc, vc, bt, cl))
+    with pytest.raises(ValueError, match="batch size must match"):
+        paged_attention_decode(q, kc, vc, bt[:1], cl, 0.125)
+    with pytest.raises(ValueError):
+        paged_attention_decode(q.float(), kc, vc, bt, cl, 0.125)
+    with pytest.raises(ValueError, match="multiple"):
+        paged_attention_decode(q[:, :7], kc, vc, bt, cl, 0.125)  # 7 query heads over 2 kv heads
+    with pytest.raises(ValueError):
+        paged_attention_decode(q, kc, vc[:, :1], bt, cl, 0.125)
+
+
+def test_cuda_graph_capture_and_replay():
+    w = make_workload("cfg2-qwen2-0.5b", device=DEV)
+    kc, vc = w.key_cache.clone(), w.value_cache.clone()
+    out = torch.empty_like(w.query)
+    static_q = w.query.clone()
+    args = (static_q, kc, vc, w.block_tables, w.context_lens, w.scale, w.slot_mapping, w.new_key, w.new_value)
+    paged_attention_decode(*args, out=out)  # eager call sizes the workspace
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        paged_attention_decode(*args, out=out)
+    new_q = torch.randn_like(w.query.float()).to(w.query.dtype)
+    static_q.copy_(new_q)
+    g.replay()
+    torch.cuda.synchronize()
+    eager = paged_attention_decode(new_q, kc, vc, w.block_tables, w.context_lens, w.scale)
+    assert torch.equal(out, eager)

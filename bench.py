@@ -23,6 +23,7 @@ sample of the same workload instead.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import math
 import os
@@ -149,6 +150,8 @@ def run_reference(args) -> None:
     from oracle import oracle
 
     spec = SPECS[args.workload]
+    if args.batch:
+        spec = dataclasses.replace(spec, batch=args.batch)
     GB = spec.batch * world
     lens_all = sample_lengths(spec, GB)
     g = torch.Generator().manual_seed(4242)
@@ -199,6 +202,8 @@ def main() -> None:
     ap.add_argument("--workload", default="cfg3-llama3-8b")
     ap.add_argument("--cpu-rows", type=int, default=16, help="rows in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the workload's per-GPU batch (smaller cases for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -222,6 +227,8 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
     spec = SPECS[args.workload]
+    if args.batch:
+        spec = dataclasses.replace(spec, batch=args.batch)
     GB = spec.batch * world
     lens = sample_lengths(spec, GB) + spec.q_len
     if spec.length_dist == "prefix":

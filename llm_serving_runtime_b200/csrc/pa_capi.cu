@@ -127,16 +127,18 @@ DecodeShape decode_shape(int Hq, int Hkv, int q_len) {
   return s;
 }
 
-size_t workspace_bytes_impl(int B, int Hkv, int NMG, int slot_rows, int D, int nw_total) {
-  return pa::kWsHeaderBytes + pa::ws_counter_bytes(B, Hkv, NMG) +
-         pa::ws_partial_bytes(nw_total, slot_rows, D);
+// Workspace: [status word | pad to 256][nw_total merge counters][2*nw_total partial
+// slots].  The counters sit at a fixed offset whatever the call's shape, so a
+// workspace shared by calls of different shapes keeps them at zero.
+size_t workspace_bytes_impl(int slot_rows, int D, int nw_total) {
+  return pa::kWsHeaderBytes + pa::ws_counter_bytes(nw_total) + pa::ws_partial_bytes(nw_total, slot_rows, D);
 }
 
 }  // namespace
 
 namespace pa {
 
-size_t ws_counter_bytes(int B, int Hkv, int NMG) { return round_up((size_t)B * Hkv * NMG * 4); }
+size_t ws_counter_bytes(int nw_total) { return round_up((size_t)nw_total * 4); }
 
 size_t ws_partial_bytes(int nw_total, int slot_rows, int D) {
   return round_up((size_t)2 * nw_total * slot_rows * (2 + D) * 4);
@@ -159,8 +161,7 @@ size_t pa_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num
   if (device_info(device, &info) != PA_OK) return 0;
   const DecodeShape s = decode_shape(num_q_heads, num_kv_heads, q_len);
   if (dtype == PA_DTYPE_FLOAT32) return pa::kWsHeaderBytes;
-  return workspace_bytes_impl(batch, num_kv_heads, s.NMG, s.slot_rows, head_dim,
-                              info->num_sms * pa::kDecodeWarps);
+  return workspace_bytes_impl(s.slot_rows, head_dim, info->num_sms * pa::kDecodeWarps);
 }
 
 int pa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
@@ -343,12 +344,12 @@ int pa_decode(const pa_decode_args* a, void* stream) {
     return fail(PA_ERR_UNSUPPORTED, "fp16/bf16 decode needs a power-of-two block_size in [8, 256], got %d", bs);
   const int grid = info->num_sms;
   p.nw_total = grid * pa::kDecodeWarps;
-  const size_t need = workspace_bytes_impl(p.B, p.Hkv, p.NMG, p.slot_rows, D, p.nw_total);
+  const size_t need = workspace_bytes_impl(p.slot_rows, D, p.nw_total);
   if (a->workspace_bytes < need)
     return fail(PA_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", a->workspace_bytes, need);
   char* ws = static_cast<char*>(a->workspace);
   p.counters = reinterpret_cast<int32_t*>(ws + pa::kWsHeaderBytes);
-  p.partials = reinterpret_cast<float*>(ws + pa::kWsHeaderBytes + pa::ws_counter_bytes(p.B, p.Hkv, p.NMG));
+  p.partials = reinterpret_cast<float*>(ws + pa::kWsHeaderBytes + pa::ws_counter_bytes(p.nw_total));
 
   // Ring depth: as many 16-token stages per warp as shared memory allows (2..8).
   const size_t budget = (size_t)info->max_smem_optin - 64;  // static shared memory of the kernel

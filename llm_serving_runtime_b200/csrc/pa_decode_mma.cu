@@ -14,7 +14,8 @@
 //    to within one unit.  A slice that covers a whole (sequence, head) writes
 //    the output directly; a row cut by a slice boundary leaves (m, l, acc)
 //    partials in the workspace, and the last warp to finish that row merges
-//    them with a log-sum-exp reduction (arrival counter, reset after use).
+//    them with a log-sum-exp reduction (arrival counter, reset after use; one
+//    counter per warp of the grid, so the workspace layout is shape-independent).
 //  * GQA packing: the G query heads (times q_len query tokens) that read one KV
 //    head form the 16 rows of an m16n8k16 tile, so each K/V tile is read from
 //    HBM once for the whole group.
@@ -502,7 +503,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         const int gw1 = (int)(((row_start + 1) * nw_eff - 1) / W);
         const int gw2 = (int)((row_stop * nw_eff - 1) / W);
         const int npieces = gw2 - gw1 + 1;
-        const int row_id = b * rows_per_b + cc.r;
+        // A split row's counter is indexed by the warp that holds its last unit:
+        // that warp starts inside the row, so no other split row ends there.
+        // The counter region thus depends only on the grid, not on the batch.
+        const int row_id = gw2;
         int old = 0;
         if (lane == 0) old = atomicAdd(&p.counters[row_id], 1);
         old = __shfl_sync(0xffffffffu, old, 0);

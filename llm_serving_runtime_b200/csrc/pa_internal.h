@@ -40,7 +40,7 @@ struct DecodeParams {
   float scale;       // softmax scale
   float scale_log2;  // scale * log2(e)
   uint32_t* status;  // device error word
-  int32_t* counters; // [B * Hkv * NMG] merge arrival counters (kept at zero between calls)
+  int32_t* counters; // [nw_total] merge arrival counters (kept at zero between calls)
   float* partials;   // [2 * nw_total] slots of (m, l, O) partial states
   int32_t slot_rows; // rows stored per partial slot
   int32_t nw_total;  // warps in the grid
@@ -69,7 +69,7 @@ struct AppendParams {
 };
 
 // Workspace layout helpers (bytes).
-size_t ws_counter_bytes(int B, int Hkv, int NMG);
+size_t ws_counter_bytes(int nw_total);
 size_t ws_partial_bytes(int nw_total, int slot_rows, int D);
 
 // Launchers (return cudaError_t of the launch).

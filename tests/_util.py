@@ -41,3 +41,29 @@ def max_err(out: torch.Tensor, ref_f32: torch.Tensor) -> float:
     """Max abs difference with the fp32 oracle rounded to the output dtype (the
     reference rounds its fp32 result the same way, paged_attention_triton.py:703)."""
     return (out.float().cpu() - ref_f32.to(out.dtype).float().cpu()).abs().max().item()
+
+
+def ulp(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Spacing of ``dtype`` values at |x| (one rounding step of the output)."""
+    a = x.abs().float().clamp_min(torch.finfo(dtype).tiny)
+    return torch.exp2(torch.floor(torch.log2(a))) * torch.finfo(dtype).eps
+
+
+def excess_err(out: torch.Tensor, ref_f32: torch.Tensor) -> float:
+    """How far the output is beyond the bar.
+
+    Both sides round an fp32 value to the output dtype, so where one rounding
+    step of the dtype is itself coarser than the north-star tolerance (bf16
+    outputs of magnitude >= 0.5, whose step is 2^-8 = 3.9e-3) a one-step
+    disagreement is the finest resolvable answer.  The bar per element is
+    max(TOL[dtype], one step of the dtype at the reference value).
+    Returns max(err - bar); <= 0 means within the bar.
+    """
+    o = out.float().cpu()
+    r = ref_f32.float().cpu()
+    rr = r.to(out.dtype).float()
+    err = (o - rr).abs()
+    bar = torch.full_like(err, TOL[out.dtype])
+    if out.dtype != torch.float32:
+        bar = torch.maximum(bar, ulp(rr, out.dtype) * 1.0001)
+    return (err - bar).max().item()

@@ -149,6 +149,27 @@ PA_API int pa_kv_append(const pa_kv_append_args* args, void* stream);
  * :414-457 (log-sum-exp combine). */
 PA_API int pa_decode(const pa_decode_args* args, void* stream);
 
+/* Size of the scratch array behind pa_decode_static_workspace (16 MiB). */
+#define PA_STATIC_WORKSPACE_BYTES (16u << 20)
+
+/* pa_decode for callers that cannot allocate device memory.  No counterpart in
+ * the reference (its decode allocates scratch on first use per shape).
+ * Takes the same arguments as pa_decode but ignores args->workspace and
+ * args->workspace_bytes: the scratch is a 16 MiB __device__ array inside this
+ * library, which every GPU that loads the library holds until the process
+ * exits.  Nothing is allocated: a plugin host that hands its kernels only
+ * inputs and outputs, or a serving loop that has given all free HBM to the KV
+ * pool, can call it.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, that device current) and should come before
+ * any stream capture.  Every call shares the array: each clears the error word
+ * and merge counters on its stream before the decode, and calls that overlap
+ * on the GPU race.  Shapes needing more scratch than PA_STATIC_WORKSPACE_BYTES
+ * (pa_decode_workspace_bytes) are rejected with PA_ERR_WORKSPACE; on a 148-SM
+ * B200 that is more than 13 query rows per KV head (G * q_len) at head_dim 128.
+ * The kernels still skip invalid block ids, but their device error word stays
+ * inside the array: this entry point reports host-side errors only. */
+PA_API int pa_decode_static_workspace(const pa_decode_args* args, void* stream);
+
 /* Bytes of workspace pa_decode needs on `device` for these shapes.
  * Replaces the scratch caches _decode_scratch_buffers / _direct_out_buffer
  * (runtime/phase2/paged_attention_triton.py:90-115); unlike them the output is

@@ -28,9 +28,12 @@ PA_DEVERR_TABLE_UNDERRUN = 0x2
 PA_DEVERR_SLOT_RANGE = 0x4
 PA_DEVERR_WAIT_TIMEOUT = 0x8
 
+PA_STATIC_WORKSPACE_BYTES = 16 << 20
+
 EXPORTED_SYMBOLS = (
     "pa_kv_append",
     "pa_decode",
+    "pa_decode_static_workspace",
     "pa_decode_workspace_bytes",
     "pa_workspace_init",
     "pa_read_device_errors",
@@ -116,6 +119,8 @@ def load() -> ctypes.CDLL:
         lib.pa_kv_append.argtypes = [ctypes.POINTER(KvAppendArgs), _vp]
         lib.pa_decode.restype = ctypes.c_int
         lib.pa_decode.argtypes = [ctypes.POINTER(DecodeArgs), _vp]
+        lib.pa_decode_static_workspace.restype = ctypes.c_int
+        lib.pa_decode_static_workspace.argtypes = [ctypes.POINTER(DecodeArgs), _vp]
         lib.pa_decode_workspace_bytes.restype = _sz
         lib.pa_decode_workspace_bytes.argtypes = [_i32, _i32, _i32, _i32, _i32, _i32, _i32]
         lib.pa_workspace_init.restype = ctypes.c_int

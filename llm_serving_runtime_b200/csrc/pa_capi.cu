@@ -138,6 +138,8 @@ size_t workspace_bytes_impl(int slot_rows, int D, int nw_total) {
 
 namespace pa {
 
+int set_last_error(int status, const char* msg) { return fail(status, "%s", msg); }
+
 size_t ws_counter_bytes(int nw_total) { return round_up((size_t)nw_total * 4); }
 
 size_t ws_partial_bytes(int nw_total, int slot_rows, int D) {

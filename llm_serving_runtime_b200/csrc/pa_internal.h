@@ -68,6 +68,9 @@ struct AppendParams {
   uint32_t* error_flags;
 };
 
+// Record the message pa_last_error() returns on this host thread; returns status.
+int set_last_error(int status, const char* msg);
+
 // Workspace layout helpers (bytes).
 size_t ws_counter_bytes(int nw_total);
 size_t ws_partial_bytes(int nw_total, int slot_rows, int D);

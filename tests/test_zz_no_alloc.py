@@ -1,0 +1,87 @@
+"""pa_decode_static_workspace: the decode entry point for callers that cannot
+allocate device memory (a plugin host that passes only inputs and outputs, a
+serving loop whose free HBM all belongs to the KV pool).  Its scratch is a
+fixed array inside the library, so it takes no workspace argument.
+
+Called through the C ABI (ctypes) and compared with the regular entry point
+pa_decode (caller-provided workspace) on two calls in a row with different
+inputs, so scratch left by the first call must not leak into the second.
+Collected last on purpose; it also passes alone in a fresh process.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+from _util import TOL, max_err
+from llm_serving_runtime_b200 import _lib, paged_attention_decode
+from llm_serving_runtime_b200.workloads import make_workload
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+_DT = {torch.float32: _lib.PA_DTYPE_FLOAT32, torch.float16: _lib.PA_DTYPE_FLOAT16,
+       torch.bfloat16: _lib.PA_DTYPE_BFLOAT16}
+
+
+def _view(t):
+    return _lib.CacheView(t.data_ptr(), t.shape[0], t.stride(0), t.stride(1), t.stride(2))
+
+
+def _args(w, out) -> _lib.DecodeArgs:
+    a = _lib.DecodeArgs()
+    q = w.query
+    a.query = q.data_ptr()
+    a.query_stride_b, a.query_stride_h, a.query_stride_t = q.stride(0), q.stride(1), q.stride(2)
+    a.key_cache, a.value_cache = _view(w.key_cache), _view(w.value_cache)
+    a.block_tables = w.block_tables.data_ptr()
+    a.block_table_stride = w.block_tables.stride(0)
+    a.max_blocks = w.block_tables.shape[1]
+    a.context_lens = w.context_lens.data_ptr()
+    a.len_offset = w.q_len
+    a.out = out.data_ptr()
+    a.out_stride_b, a.out_stride_h, a.out_stride_t = out.stride(0), out.stride(1), out.stride(2)
+    a.batch, a.q_len = q.shape[0], q.shape[2]
+    a.num_q_heads, a.num_kv_heads = q.shape[1], w.key_cache.shape[1]
+    a.head_dim, a.block_size = q.shape[3], w.key_cache.shape[2]
+    a.dtype = _DT[q.dtype]
+    a.scale = w.scale
+    a.workspace = None      # ignored by the static-workspace entry point
+    a.workspace_bytes = 0
+    return a
+
+
+def _static_decode(w) -> torch.Tensor:
+    out = torch.empty_like(w.query)
+    args = _args(w, out)
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    rc = _lib.load().pa_decode_static_workspace(ctypes.byref(args), stream)
+    assert rc == _lib.PA_OK, _lib.last_error()
+    return out
+
+
+def test_static_workspace_matches_pa_decode_on_two_calls_in_a_row():
+    torch.cuda.set_device(DEV)
+    first = make_workload("cfg3-llama3-8b", device=DEV, rows=list(range(48)))
+    second = make_workload("cfg5-llama3-70b", device=DEV, rows=list(range(24)))
+    for w in (first, second):
+        expected = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables,
+                                          w.context_lens, w.scale)
+        got = _static_decode(w)
+        torch.cuda.synchronize()
+        err = max_err(got, expected.float())
+        assert err <= TOL[w.query.dtype], f"{w.spec.name}: max abs err {err}"
+
+
+def test_static_workspace_rejects_shapes_beyond_its_size():
+    torch.cuda.set_device(DEV)
+    # 4 query tokens x 4 query heads per KV head at head_dim 128: 16 rows of
+    # partial state per warp, more scratch than the 16 MiB array holds.
+    w = make_workload("cfg4-prefix-verify", device=DEV, rows=list(range(4)))
+    out = torch.empty_like(w.query)
+    args = _args(w, out)
+    rc = _lib.load().pa_decode_static_workspace(ctypes.byref(args), torch.cuda.current_stream(DEV).cuda_stream)
+    assert rc == _lib.PA_ERR_WORKSPACE
+    assert "static workspace holds" in _lib.last_error()

@@ -126,12 +126,12 @@ def _dist_setup():
     return world, rank, local
 
 
-def _traffic_from_profiles(workload: str) -> float | None:
-    """DRAM bytes per decode launch recorded from an ncu capture (profiles/*.md,
-    line 'dram_bytes_per_launch[<workload>]: <bytes>'), or None."""
+def _traffic_ratio_from_profiles(workload: str) -> float | None:
+    """DRAM bytes / algorithmic bytes of the decode launch from an ncu capture
+    (profiles/*.md, line 'dram_traffic_ratio[<workload>]: <ratio>'), or None."""
     for p in sorted((REPO / "profiles").glob("*.md")):
         for line in p.read_text().splitlines():
-            key = f"dram_bytes_per_launch[{workload}]:"
+            key = f"dram_traffic_ratio[{workload}]:"
             if line.strip().startswith(key):
                 try:
                     return float(line.split(":", 1)[1].strip().split()[0])
@@ -204,6 +204,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the workload's per-GPU batch (smaller cases for ncu captures)")
+    ap.add_argument("--shard", choices=["auto", "seq", "head"], default="auto",
+                    help="multi-GPU layout: sequences (weak scaling) or KV heads + NCCL all-gather "
+                         "(strong scaling); auto = heads for cfg5-llama3-70b, sequences otherwise")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -215,8 +218,8 @@ def main() -> None:
     import torch.distributed as dist
 
     from llm_serving_runtime_b200 import paged_attention_decode
-    from llm_serving_runtime_b200.workloads import SPECS, algorithmic_bytes, lpt_partition, make_workload, \
-        sample_lengths
+    from llm_serving_runtime_b200.sharding import HeadShardedDecode, kv_head_range, shard_sequences
+    from llm_serving_runtime_b200.workloads import SPECS, algorithmic_bytes, make_workload, sample_lengths
 
     world, rank, local = _dist_setup()
     if world != args.gpus:
@@ -229,21 +232,30 @@ def main() -> None:
     spec = SPECS[args.workload]
     if args.batch:
         spec = dataclasses.replace(spec, batch=args.batch)
-    GB = spec.batch * world
-    lens = sample_lengths(spec, GB) + spec.q_len
-    if spec.length_dist == "prefix":
-        per_group = spec.batch // spec.prefix_groups
-        groups = [list(range(i, i + per_group)) for i in range(0, GB, per_group)]
-        shards = lpt_partition(lens, world, groups=groups)
+    shard = args.shard
+    if shard == "auto":
+        shard = "head" if (world > 1 and args.workload == "cfg5-llama3-70b") else "seq"
+    if shard == "head":
+        # every rank holds its KV heads of the whole batch; outputs all-gathered
+        GB = spec.batch
+        w = make_workload(spec, device=dev, kv_heads=kv_head_range(spec.num_kv_heads, world, rank))
+        gather = HeadShardedDecode()
     else:
-        shards = lpt_partition(lens, world)
-    w = make_workload(spec, device=dev, rows=shards[rank], global_batch=GB)
+        GB = spec.batch * world
+        lens = sample_lengths(spec, GB) + spec.q_len
+        group = spec.batch // spec.prefix_groups if spec.length_dist == "prefix" else 0
+        shards = shard_sequences(lens.tolist(), world, group_size=group)
+        w = make_workload(spec, device=dev, rows=shards[rank], global_batch=GB)
+        gather = None
     B, q = w.batch, w.q_len
     out = torch.empty_like(w.query)
 
     def step():
-        paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
-                               w.slot_mapping, w.new_key, w.new_value, out=out)
+        if gather is not None:
+            return gather(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                          w.slot_mapping, w.new_key, w.new_value, out=out)
+        return paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens,
+                                      w.scale, w.slot_mapping, w.new_key, w.new_value, out=out)
 
     def barrier():
         if world > 1:
@@ -273,11 +285,11 @@ def main() -> None:
     total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
     tokens_all = torch.tensor([B * q], device=dev, dtype=torch.float64)
-    if world > 1:
+    if world > 1 and shard == "seq":
         dist.all_reduce(tokens_all)
     tokens_per_step = float(tokens_all.item())
     value = tokens_per_step / (ms_per_step / 1e3)
-    gpu_launches = 2 * args.steps  # pa_kv_append + pa_decode per step
+    gpu_launches = 2 * args.steps  # pa_kv_append + pa_decode per step (+ one NCCL all-gather in head mode)
 
     # ---- decode kernel alone, for the roofline (events around each launch) ----
     n_dec = max(20, min(args.steps, 100))
@@ -301,7 +313,8 @@ def main() -> None:
     host = {k: getattr(w, k).cpu().pin_memory() for k in
             ("query", "new_key", "new_value", "slot_mapping", "context_lens", "block_tables")}
     dev_in = {k: torch.empty_like(getattr(w, k)) for k in host}
-    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    full_out_shape = (B, spec.num_q_heads, q, spec.head_dim) if shard == "head" else tuple(out.shape)
+    host_out = torch.empty(full_out_shape, dtype=out.dtype, pin_memory=True)
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = host_out.numel() * host_out.element_size()
     n_e2e = max(10, min(args.steps, 100))
@@ -309,10 +322,10 @@ def main() -> None:
     def e2e_step():
         for k, v in host.items():
             dev_in[k].copy_(v, non_blocking=True)
-        paged_attention_decode(dev_in["query"], w.key_cache, w.value_cache, dev_in["block_tables"],
-                               dev_in["context_lens"], w.scale, dev_in["slot_mapping"], dev_in["new_key"],
-                               dev_in["new_value"], out=out)
-        host_out.copy_(out, non_blocking=True)
+        args_ = (dev_in["query"], w.key_cache, w.value_cache, dev_in["block_tables"], dev_in["context_lens"],
+                 w.scale, dev_in["slot_mapping"], dev_in["new_key"], dev_in["new_value"])
+        res = gather(*args_, out=out) if gather is not None else paged_attention_decode(*args_, out=out)
+        host_out.copy_(res, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -340,7 +353,8 @@ def main() -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
-    traffic = _traffic_from_profiles(args.workload)
+    ratio = _traffic_ratio_from_profiles(args.workload)
+    traffic = None if ratio is None else ratio * dec_bytes
     line = {
         "metric": METRIC,
         "value": value,
@@ -350,7 +364,7 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if shard == "head" else "weak",
         "vs_baseline": None,
         "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[spec.dtype],
         "data": "synthetic (seeded; random block placement)",
@@ -358,7 +372,8 @@ def main() -> None:
             "workload": args.workload, "global_batch": GB, "q_len": q, "num_q_heads": spec.num_q_heads,
             "num_kv_heads": spec.num_kv_heads, "head_dim": spec.head_dim, "block_size": spec.block_size,
             "context_lens": f"{spec.length_dist} [{spec.length_lo}, {spec.length_hi}]",
-            "parallelism": f"seq-shard{world}" if world > 1 else "single",
+            "parallelism": (f"kvhead-shard{world}+allgather" if shard == "head" else f"seq-shard{world}")
+            if world > 1 else "single",
             "l2": "inputs larger than L2 (no flush)",
             "bytes_per_call": call_bytes,
         },

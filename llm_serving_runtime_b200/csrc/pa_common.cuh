@@ -1,8 +1,8 @@
 // pa_common.cuh — shared device helpers for the sm_100a paged-decode kernels.
 //
 // Thin inline-PTX wrappers for the pieces the kernels use: mbarriers with
-// transaction counts, 4-D TMA tile loads (cp.async.bulk.tensor, never with
-// cluster multicast), ldmatrix, m16n8k16 tensor-core MMA, ex2, and programmatic
+// transaction counts, 4-D TMA tile loads (cp.async.bulk.tensor, each CTA for
+// itself only), ldmatrix, m16n8k16 tensor-core MMA, ex2, and programmatic
 // dependent launch.  Every wait is bounded (PA_WAIT_LIMIT_CYCLES).
 #pragma once
 

@@ -20,7 +20,7 @@
 //    head form the 16 rows of an m16n8k16 tile, so each K/V tile is read from
 //    HBM once for the whole group.
 //  * Each warp is a self-fed engine: its lane 0 issues 4-D TMA tile loads
-//    (128-byte swizzle, no multicast) of the unit's K and V tiles into a ring of
+//    (128-byte swizzle, each CTA loading only for itself) of the unit's K and V tiles into a ring of
 //    `stages` shared-memory slots tracked by mbarriers; the warp keeps `stages`
 //    units in flight while it computes the oldest one.  Block-table entries are
 //    fetched 32 at a time with one coalesced load and shuffled to lane 0.

@@ -330,8 +330,8 @@ int pa_decode(const pa_decode_args* a, void* stream) {
   cudaStream_t strm = static_cast<cudaStream_t>(stream);
 
   if (dtype == PA_DTYPE_FLOAT32) {
-    if (D != 32 && D != 64 && D != 128 && D != 256)
-      return fail(PA_ERR_UNSUPPORTED, "fp32 decode supports head_dim 32/64/128/256, got %d", D);
+    if (D != 32 && D != 64 && D != 128)
+      return fail(PA_ERR_UNSUPPORTED, "fp32 decode supports head_dim 32/64/128, got %d", D);
     if (!aligned_ptr(a->key_cache.data, 4) || !aligned_ptr(a->value_cache.data, 4))
       return fail(PA_ERR_UNSUPPORTED, "cache base must be 4-byte aligned");
     e = pa::launch_decode_f32(p, pdl, strm);

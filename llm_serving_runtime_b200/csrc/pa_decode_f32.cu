@@ -1,16 +1,22 @@
 // pa_decode_f32.cu — paged decode attention for fp32 caches (CUDA cores).
 //
 // fp32 must match the reference to 1e-5, so it stays off the tensor cores
-// (TF32 would not).  The kernel follows the reference's per-row CPU algorithm
-// block by block (runtime/phase2/paged_attention_triton.py:663-704):
-//   for each cache block: scores = (q . k) * scale over the block's tokens,
-//   m_new = max(m, max(scores)), p = exp(scores - m_new), alpha = exp(m - m_new),
-//   l = l * alpha + sum(p), acc = acc * alpha + p @ v;   out = acc / l
-// with a causal limit for query token t of L - q_len + t.
-// One CTA serves one (sequence, kv head); each warp takes query rows of the GQA
-// group in turn; a lane scores one token of the block and owns D/32 output dims.
-// The fp32 configurations are small (launch-bound), so this kernel favours a
-// direct restatement over bandwidth tricks.
+// (TF32 would not).  The math is the reference's per-row CPU algorithm
+// (runtime/phase2/paged_attention_triton.py:663-704), applied to chunks of at
+// most 16 tokens of one cache block:
+//   scores = (q . k) * scale,  m_new = max(m, max(scores)),
+//   p = exp(scores - m_new),   alpha = exp(m - m_new),
+//   l = l * alpha + sum(p),    acc = acc * alpha + p @ v;      out = acc / l
+// with the causal limit L - q_len + t for query token t.
+//
+// One CTA serves one (sequence, kv head).  Its warps take the sequence's
+// blocks in turn (block w, w + NW, ...), each keeping (m, l, acc) for every
+// query row of the GQA group (up to 16 rows per pass); a chunk's K and V are
+// staged in shared memory with a padded row pitch (D + 1 floats, so lanes
+// reading different tokens hit different banks).  Lanes score one token each
+// for all rows, then own D/32 output dims for the P.V update.  At the end the
+// warps' states are merged with the log-sum-exp rule.  The fp32 configurations
+// are small, so this kernel aims at latency: many warps in flight per row.
 #include <math.h>
 
 #include "pa_common.cuh"
@@ -18,18 +24,34 @@
 
 namespace pa {
 
+namespace {
+constexpr int kF32Warps = 8;
+constexpr int kF32Rows = 16;   // query rows per pass
+constexpr int kF32Chunk = 16;  // tokens per staged chunk
+}  // namespace
+
 template <int DPL>  // head_dim / 32
-__global__ void __launch_bounds__(128) decode_f32_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const DecodeParams p) {
   constexpr int D = DPL * 32;
-  constexpr int kWarps = 4;
-  __shared__ float s_q[kWarps][D];
+  constexpr int PITCH = D + 1;
+  extern __shared__ float f32_smem[];
+  // [rows][D] queries | (m, l) per warp and row | per warp: K chunk, V chunk
+  // [kF32Chunk][PITCH] and P [rows][kF32Chunk].  After its last block a warp
+  // reuses its own K/V chunk area for its [rows][D] accumulator.
+  constexpr int kWarpFloats = 2 * kF32Chunk * PITCH + kF32Rows * kF32Chunk;
+  static_assert(kF32Rows * D <= 2 * kF32Chunk * PITCH, "accumulator must fit the staging area");
+  float* s_q = f32_smem;
+  float* s_ml = s_q + kF32Rows * D;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  float* s_k = s_ml + kF32Warps * 2 * kF32Rows + warp * kWarpFloats;
+  float* s_v = s_k + kF32Chunk * PITCH;
+  float* s_p = s_v + kF32Chunk * PITCH;
 
   pdl_wait_previous();
 
   const int b = blockIdx.x / p.Hkv;
   const int h = blockIdx.x - b * p.Hkv;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
 
   int L = p.context_lens[b] + p.len_offset;
   const int cap = p.max_blocks * p.bs;
@@ -38,99 +60,190 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(const DecodeParams p) {
     L = cap;
   }
   if (L < 0) L = 0;
+  const int first_limit = L - p.q_len;  // last token row t=0 may attend
+  const int ntok_max = L;               // tokens any row may attend
+  const int nblk = (ntok_max + p.bs - 1) / p.bs;
 
   const float* kc = static_cast<const float*>(p.k_cache);
   const float* vc = static_cast<const float*>(p.v_cache);
 
-  for (int qr = warp; qr < p.GQ; qr += kWarps) {
-    const int g = qr / p.q_len;
-    const int t = qr - g * p.q_len;
-    const int head = h * p.G + g;
-    const float* qp = static_cast<const float*>(p.q) + (long long)b * p.q_sb +
-                      (long long)head * p.q_sh + (long long)t * p.q_st;
+  for (int r0 = 0; r0 < p.GQ; r0 += kF32Rows) {
+    const int R = min(kF32Rows, p.GQ - r0);
+    __syncthreads();  // previous pass's merge area and queries are free
+    for (int i = threadIdx.x; i < R * D; i += blockDim.x) {
+      const int r = i / D, d = i - (i / D) * D;
+      const int qr = r0 + r;
+      const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+      s_q[r * D + d] = static_cast<const float*>(p.q)[(long long)b * p.q_sb + (long long)(h * p.G + g) * p.q_sh +
+                                                     (long long)t * p.q_st + d];
+    }
+    __syncthreads();
+
+    float m[kF32Rows], l[kF32Rows], acc[kF32Rows][DPL];
 #pragma unroll
-    for (int k = 0; k < DPL; ++k) s_q[warp][lane + 32 * k] = qp[lane + 32 * k];
-    __syncwarp();
-
-    int ntok = L - p.q_len + t + 1;  // tokens 0 .. L - q_len + t
-    if (ntok > L) ntok = L;
-    if (ntok < 0) ntok = 0;
-
-    float m = -INFINITY, l = 0.f;
-    float acc[DPL];
+    for (int r = 0; r < kF32Rows; ++r) {
+      m[r] = -INFINITY;
+      l[r] = 0.f;
 #pragma unroll
-    for (int k = 0; k < DPL; ++k) acc[k] = 0.f;
+      for (int j = 0; j < DPL; ++j) acc[r][j] = 0.f;
+    }
 
-    for (int blk = 0; blk * p.bs < ntok; ++blk) {
+    for (int blk = warp; blk < nblk; blk += kF32Warps) {
       const int phys = p.block_tables[(long long)b * p.bt_stride + blk];
       if (phys < 0 || phys >= p.num_blocks) {
         if (lane == 0) raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
         continue;
       }
-      const int take = min(p.bs, ntok - blk * p.bs);
+      const int take = min(p.bs, ntok_max - blk * p.bs);
       const float* kb = kc + (long long)phys * p.k_sblk + (long long)h * p.k_sh;
       const float* vb = vc + (long long)phys * p.v_sblk + (long long)h * p.v_sh;
-      for (int c0 = 0; c0 < take; c0 += 32) {
-        const int cnt = min(32, take - c0);
-        float sc = -INFINITY;
+      for (int c0 = 0; c0 < take; c0 += kF32Chunk) {
+        const int cnt = min(kF32Chunk, take - c0);
+        const int tok0 = blk * p.bs + c0;  // absolute position of the chunk's first token
+        if (tok0 > first_limit + p.q_len - 1) break;  // no row attends past L - 1
+        __syncwarp();
+#pragma unroll 4
+        for (int t = 0; t < cnt; ++t) {
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) {
+            s_k[t * PITCH + lane + 32 * j] = kb[(long long)(c0 + t) * p.k_st + lane + 32 * j];
+            s_v[t * PITCH + lane + 32 * j] = vb[(long long)(c0 + t) * p.v_st + lane + 32 * j];
+          }
+        }
+        __syncwarp();
+        // scores: lane t scores token t for every row
+        float sc[kF32Rows];
+#pragma unroll
+        for (int r = 0; r < kF32Rows; ++r) sc[r] = 0.f;
         if (lane < cnt) {
-          const float* kr = kb + (long long)(c0 + lane) * p.k_st;
-          float dot = 0.f;
-#pragma unroll 8
-          for (int d = 0; d < D; ++d) dot = fmaf(s_q[warp][d], kr[d], dot);
-          sc = dot * p.scale;
+          const float* kr = s_k + lane * PITCH;
+#pragma unroll 4
+          for (int d = 0; d < D; ++d) {
+            const float kd = kr[d];
+#pragma unroll
+            for (int r = 0; r < kF32Rows; ++r)
+              if (r < R) sc[r] = fmaf(s_q[r * D + d], kd, sc[r]);
+          }
         }
-        float bm = sc;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
-        const float m_new = fmaxf(m, bm);
-        const float alpha = (m == -INFINITY) ? 0.f : expf(m - m_new);
-        const float pl = (lane < cnt) ? expf(sc - m_new) : 0.f;
-        float ps = pl;
+        for (int r = 0; r < kF32Rows; ++r) {
+          if (r >= R) break;
+          const int qr = r0 + r;
+          const int t_q = qr - (qr / p.q_len) * p.q_len;
+          const int lim = first_limit + t_q;  // last attendable position of this row
+          const bool valid = lane < cnt && tok0 + lane <= lim;
+          float s = valid ? sc[r] * p.scale : -INFINITY;
+          float bm = s;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-        l = l * alpha + ps;
+          for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+          if (bm == -INFINITY) {  // nothing attendable for this row in this chunk
+            if (lane < kF32Chunk) s_p[r * kF32Chunk + lane] = 0.f;
+            continue;
+          }
+          const float m_new = fmaxf(m[r], bm);
+          const float alpha = (m[r] == -INFINITY) ? 0.f : expf(m[r] - m_new);
+          const float pv = valid ? expf(s - m_new) : 0.f;
+          float ps = pv;
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) acc[k] *= alpha;
-        for (int tt = 0; tt < cnt; ++tt) {
-          const float pt = __shfl_sync(0xffffffffu, pl, tt);
-          const float* vr = vb + (long long)(c0 + tt) * p.v_st;
+          for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+          l[r] = l[r] * alpha + ps;
+          m[r] = m_new;
 #pragma unroll
-          for (int k = 0; k < DPL; ++k) acc[k] = fmaf(pt, vr[lane + 32 * k], acc[k]);
+          for (int j = 0; j < DPL; ++j) acc[r][j] *= alpha;
+          if (lane < kF32Chunk) s_p[r * kF32Chunk + lane] = pv;
         }
-        m = m_new;
+        __syncwarp();
+        // acc += P V over the chunk's tokens
+        for (int t = 0; t < cnt; ++t) {
+          float vd[DPL];
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) vd[j] = s_v[t * PITCH + lane + 32 * j];
+#pragma unroll
+          for (int r = 0; r < kF32Rows; ++r) {
+            if (r < R) {
+              const float pt = s_p[r * kF32Chunk + t];
+#pragma unroll
+              for (int j = 0; j < DPL; ++j) acc[r][j] = fmaf(pt, vd[j], acc[r][j]);
+            }
+          }
+        }
       }
     }
 
-    float* op = static_cast<float*>(p.out) + (long long)b * p.o_sb + (long long)head * p.o_sh +
-                (long long)t * p.o_st;
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-    for (int k = 0; k < DPL; ++k) op[lane + 32 * k] = acc[k] * inv;
+    // ---- merge the warps' states (log-sum-exp) and store ----
     __syncwarp();
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r) {
+      if (r < R) {
+        if (lane == 0) {
+          s_ml[(warp * 2) * kF32Rows + r] = m[r];
+          s_ml[(warp * 2 + 1) * kF32Rows + r] = l[r];
+        }
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) s_k[r * D + lane + 32 * j] = acc[r][j];
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < R * D; i += blockDim.x) {
+      const int r = i / D, d = i - (i / D) * D;
+      float M = -INFINITY;
+      for (int w = 0; w < kF32Warps; ++w) M = fmaxf(M, s_ml[(w * 2) * kF32Rows + r]);
+      float lsum = 0.f, a = 0.f;
+      if (M != -INFINITY) {
+        for (int w = 0; w < kF32Warps; ++w) {
+          const float mw = s_ml[(w * 2) * kF32Rows + r];
+          const float sc_w = (mw == -INFINITY) ? 0.f : expf(mw - M);
+          lsum += sc_w * s_ml[(w * 2 + 1) * kF32Rows + r];
+          a += sc_w * s_ml[kF32Warps * 2 * kF32Rows + w * kWarpFloats + r * D + d];
+        }
+      }
+      const int qr = r0 + r;
+      const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+      static_cast<float*>(p.out)[(long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh + (long long)t * p.o_st +
+                                 d] = lsum > 0.f ? a / lsum : 0.f;
+    }
   }
 }
 
-cudaError_t launch_decode_f32(const DecodeParams& p, bool pdl, cudaStream_t stream) {
+static size_t f32_smem_bytes(int D) {
+  const int pitch = D + 1;
+  return sizeof(float) * ((size_t)kF32Rows * D + (size_t)kF32Warps * 2 * kF32Rows +
+                          (size_t)kF32Warps * (2 * kF32Chunk * pitch + kF32Rows * kF32Chunk));
+}
+
+template <int DPL>
+static cudaError_t launch_f32_impl(const DecodeParams& p, bool pdl, cudaStream_t stream) {
+  const size_t smem = f32_smem_bytes(DPL * 32);
+  static bool prepared[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !prepared[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(decode_f32_kernel<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    prepared[dev] = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(p.B * p.Hkv));
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = 0;
+  cfg.blockDim = dim3(kF32Warps * 32);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = pdl ? attr : nullptr;
   cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, decode_f32_kernel<DPL>, p);
+}
+
+cudaError_t launch_decode_f32(const DecodeParams& p, bool pdl, cudaStream_t stream) {
   switch (p.D) {
     case 32:
-      return cudaLaunchKernelEx(&cfg, decode_f32_kernel<1>, p);
+      return launch_f32_impl<1>(p, pdl, stream);
     case 64:
-      return cudaLaunchKernelEx(&cfg, decode_f32_kernel<2>, p);
+      return launch_f32_impl<2>(p, pdl, stream);
     case 128:
-      return cudaLaunchKernelEx(&cfg, decode_f32_kernel<4>, p);
-    case 256:
-      return cudaLaunchKernelEx(&cfg, decode_f32_kernel<8>, p);
+      return launch_f32_impl<4>(p, pdl, stream);
     default:
       return cudaErrorInvalidValue;
   }

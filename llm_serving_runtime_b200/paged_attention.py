@@ -164,20 +164,38 @@ def _as_int32(t: torch.Tensor, device: torch.device, name: str) -> torch.Tensor:
     return t.to(device=device, dtype=torch.int32)
 
 
-def _with_device(device: torch.device):
-    class _Guard:
-        def __enter__(self):
-            self.prev = torch.cuda.current_device()
-            if self.prev != device.index:
-                torch.cuda.set_device(device)
-            return self
+class _with_device:
+    """Make ``device`` current for the C calls (they launch on the current device)."""
 
-        def __exit__(self, *exc):
-            if self.prev != device.index:
-                torch.cuda.set_device(self.prev)
-            return False
+    __slots__ = ("device", "prev")
 
-    return _Guard()
+    def __init__(self, device: torch.device):
+        self.device = device
+
+    def __enter__(self):
+        self.prev = torch.cuda.current_device()
+        if self.prev != self.device.index:
+            torch.cuda.set_device(self.device)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev != self.device.index:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
+_ws_bytes_cache: dict[tuple, int] = {}
+
+
+def _workspace_bytes(B: int, Hq: int, Hkv: int, q_len: int, D: int, dcode: int, dev_index: int) -> int:
+    key = (B, Hq, Hkv, q_len, D, dcode, dev_index)
+    n = _ws_bytes_cache.get(key)
+    if n is None:
+        n = _lib.load().pa_decode_workspace_bytes(B, Hq, Hkv, q_len, D, dcode, dev_index)
+        if n == 0:
+            raise RuntimeError(f"pa_decode_workspace_bytes failed: {_lib.last_error()}")
+        _ws_bytes_cache[key] = n
+    return n
 
 
 def kv_append(
@@ -314,10 +332,7 @@ def paged_attention_decode(
     lib = _lib.load()
     dcode = _DTYPE_CODE[query.dtype]
     if workspace is None:
-        need = lib.pa_decode_workspace_bytes(B, Hq, Hkv, q_len, D, dcode, device.index)
-        if need == 0:
-            raise RuntimeError(f"pa_decode_workspace_bytes failed: {_lib.last_error()}")
-        workspace = decode_workspace(device, need)
+        workspace = decode_workspace(device, _workspace_bytes(B, Hq, Hkv, q_len, D, dcode, device.index))
 
     appended = False
     if key is not None:

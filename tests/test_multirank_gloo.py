@@ -66,7 +66,7 @@ def _seq_worker(rank, world, port, out_q):
         out = torch.empty_like(w.query)
         for rows, part in gathered:
             out[torch.tensor(rows)] = part
-        out_q.put(out)
+        out_q.put(out.float().numpy())  # by value: the worker exits right after
     dist.destroy_process_group()
 
 
@@ -82,7 +82,7 @@ def _head_worker(rank, world, port, out_q):
         q, kc, vc, w.block_tables, w.context_lens, w.scale, w.slot_mapping,
         w.new_key[:, h0:h0 + hc].contiguous(), w.new_value[:, h0:h0 + hc].contiguous())
     if rank == 0:
-        out_q.put(out)
+        out_q.put(out.float().numpy())  # by value: the worker exits right after
     dist.destroy_process_group()
 
 
@@ -117,6 +117,8 @@ def _run(fn, world=2):
     for p in procs:
         p.start()
     result = q.get(timeout=120)
+    if hasattr(result, "dtype"):
+        result = torch.from_numpy(result)
     for p in procs:
         p.join(timeout=60)
         if p.is_alive():
@@ -134,13 +136,13 @@ def _reference():
 def test_sequence_sharding_reassembles_the_batch():
     out = _run(_seq_worker)
     assert isinstance(out, torch.Tensor), out
-    assert torch.equal(out, _reference())
+    assert torch.equal(out, _reference().float())
 
 
 def test_kv_head_sharding_all_gathers_the_heads():
     out = _run(_head_worker)
     assert isinstance(out, torch.Tensor), out
-    assert torch.equal(out, _reference())
+    assert torch.equal(out, _reference().float())
 
 
 def test_rank_leaving_before_the_collective_is_an_error_not_a_hang():

@@ -26,11 +26,12 @@ namespace pa {
 
 namespace {
 constexpr int kF32Warps = 8;
-constexpr int kF32Rows = 16;   // query rows per pass
 constexpr int kF32Chunk = 16;  // tokens per staged chunk
 }  // namespace
 
-template <int DPL>  // head_dim / 32
+// DPL = head_dim / 32; kF32Rows = query rows handled per pass (4, 8 or 16,
+// the smallest that holds the GQA group's G * q_len rows).
+template <int DPL, int kF32Rows>
 __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const DecodeParams p) {
   constexpr int D = DPL * 32;
   constexpr int PITCH = D + 1;
@@ -40,6 +41,7 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const Decode
   // reuses its own K/V chunk area for its [rows][D] accumulator.
   constexpr int kWarpFloats = 2 * kF32Chunk * PITCH + kF32Rows * kF32Chunk;
   static_assert(kF32Rows * D <= 2 * kF32Chunk * PITCH, "accumulator must fit the staging area");
+  static_assert(kF32Rows <= 32, "one lane per row in the merge bookkeeping");
   float* s_q = f32_smem;
   float* s_ml = s_q + kF32Rows * D;
   const int warp = threadIdx.x >> 5;
@@ -102,14 +104,16 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const Decode
         const int tok0 = blk * p.bs + c0;  // absolute position of the chunk's first token
         if (tok0 > first_limit + p.q_len - 1) break;  // no row attends past L - 1
         __syncwarp();
+        // Stage the chunk: every copy of the chunk is in flight at once.
 #pragma unroll 4
         for (int t = 0; t < cnt; ++t) {
 #pragma unroll
           for (int j = 0; j < DPL; ++j) {
-            s_k[t * PITCH + lane + 32 * j] = kb[(long long)(c0 + t) * p.k_st + lane + 32 * j];
-            s_v[t * PITCH + lane + 32 * j] = vb[(long long)(c0 + t) * p.v_st + lane + 32 * j];
+            cp_async_4(smem_addr(&s_k[t * PITCH + lane + 32 * j]), kb + (long long)(c0 + t) * p.k_st + lane + 32 * j);
+            cp_async_4(smem_addr(&s_v[t * PITCH + lane + 32 * j]), vb + (long long)(c0 + t) * p.v_st + lane + 32 * j);
           }
         }
+        cp_async_wait_all();
         __syncwarp();
         // scores: lane t scores token t for every row
         float sc[kF32Rows];
@@ -205,21 +209,21 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const Decode
   }
 }
 
-static size_t f32_smem_bytes(int D) {
+static size_t f32_smem_bytes(int D, int kF32Rows) {
   const int pitch = D + 1;
   return sizeof(float) * ((size_t)kF32Rows * D + (size_t)kF32Warps * 2 * kF32Rows +
                           (size_t)kF32Warps * (2 * kF32Chunk * pitch + kF32Rows * kF32Chunk));
 }
 
-template <int DPL>
+template <int DPL, int ROWS>
 static cudaError_t launch_f32_impl(const DecodeParams& p, bool pdl, cudaStream_t stream) {
-  const size_t smem = f32_smem_bytes(DPL * 32);
+  const size_t smem = f32_smem_bytes(DPL * 32, ROWS);
   static bool prepared[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !prepared[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_f32_kernel<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(decode_f32_kernel<DPL, ROWS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     prepared[dev] = true;
   }
@@ -233,17 +237,24 @@ static cudaError_t launch_f32_impl(const DecodeParams& p, bool pdl, cudaStream_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = pdl ? attr : nullptr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, decode_f32_kernel<DPL>, p);
+  return cudaLaunchKernelEx(&cfg, decode_f32_kernel<DPL, ROWS>, p);
+}
+
+template <int DPL>
+static cudaError_t launch_f32_rows(const DecodeParams& p, bool pdl, cudaStream_t stream) {
+  if (p.GQ <= 4) return launch_f32_impl<DPL, 4>(p, pdl, stream);
+  if (p.GQ <= 8) return launch_f32_impl<DPL, 8>(p, pdl, stream);
+  return launch_f32_impl<DPL, 16>(p, pdl, stream);
 }
 
 cudaError_t launch_decode_f32(const DecodeParams& p, bool pdl, cudaStream_t stream) {
   switch (p.D) {
     case 32:
-      return launch_f32_impl<1>(p, pdl, stream);
+      return launch_f32_rows<1>(p, pdl, stream);
     case 64:
-      return launch_f32_impl<2>(p, pdl, stream);
+      return launch_f32_rows<2>(p, pdl, stream);
     case 128:
-      return launch_f32_impl<4>(p, pdl, stream);
+      return launch_f32_rows<4>(p, pdl, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -511,36 +511,85 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         if (lane == 0) old = atomicAdd(&p.counters[row_id], 1);
         old = __shfl_sync(0xffffffffu, old, 0);
         if (old == npieces - 1) {
-          // Last arrival: log-sum-exp merge of all pieces of this row.
+          // Last arrival: log-sum-exp merge of all pieces of this row.  Lanes
+          // span the pieces for the max and the weights; each piece's partial
+          // accumulators are then read for 8 rows at a time, all loads of a
+          // piece in flight together.
           __threadfence();
           const bool gw1_first = (W * gw1 / nw_eff) == row_start;
-          for (int r = 0; r < rows_here; ++r) {
-            float M = -INFINITY;
-            for (int g2 = gw1; g2 <= gw2; ++g2) {
-              const int si = (g2 == gw1 && !gw1_first) ? 2 * g2 + 1 : 2 * g2;
-              M = fmaxf(M, __ldcg(p.partials + (long long)si * slot_floats + r));
+          auto slot_ptr = [&](int i) -> const float* {
+            const int g2 = gw1 + i;
+            const int si = (i == 0 && !gw1_first) ? 2 * g2 + 1 : 2 * g2;
+            return p.partials + (long long)si * slot_floats;
+          };
+          constexpr int RG = DPL >= 4 ? 4 : 8;  // rows merged per pass (register budget)
+          for (int rg = 0; rg < rows_here; rg += RG) {
+            float M[RG], lsum[RG], acc[RG][DPL];
+#pragma unroll
+            for (int r = 0; r < RG; ++r) {
+              M[r] = -INFINITY;
+              lsum[r] = 0.f;
+#pragma unroll
+              for (int k = 0; k < DPL; ++k) acc[r][k] = 0.f;
             }
-            const float Mb = (M == -INFINITY) ? 0.f : M;
-            float lsum = 0.f;
-            float acc[DPL];
+            for (int i = lane; i < npieces; i += 32) {
+              const float* ps = slot_ptr(i);
 #pragma unroll
-            for (int k = 0; k < DPL; ++k) acc[k] = 0.f;
-            for (int g2 = gw1; g2 <= gw2; ++g2) {
-              const int si = (g2 == gw1 && !gw1_first) ? 2 * g2 + 1 : 2 * g2;
-              const float* ps = p.partials + (long long)si * slot_floats;
-              const float w = ex2(__ldcg(ps + r) - Mb);
-              lsum += w * __ldcg(ps + p.slot_rows + r);
-              const float* po = ps + 2 * p.slot_rows + r * D;
-#pragma unroll
-              for (int k = 0; k < DPL; ++k) acc[k] += w * __ldcg(po + lane + 32 * k);
+              for (int r = 0; r < RG; ++r)
+                if (rg + r < rows_here) M[r] = fmaxf(M[r], __ldcg(ps + rg + r));
             }
-            const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-            const int qr = mg * 16 + r;
-            const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
-            T* op = static_cast<T*>(p.out) + (long long)b * p.o_sb +
-                    (long long)(h * p.G + g) * p.o_sh + (long long)t * p.o_st;
 #pragma unroll
-            for (int k = 0; k < DPL; ++k) op[lane + 32 * k] = from_float<T>(acc[k] * inv);
+            for (int r = 0; r < RG; ++r) {
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) M[r] = fmaxf(M[r], __shfl_xor_sync(0xffffffffu, M[r], o));
+              if (M[r] == -INFINITY) M[r] = 0.f;  // exponent base of an all-empty row
+            }
+            for (int i0 = 0; i0 < npieces; i0 += 32) {
+              float wgt[RG];
+              const int i = i0 + lane;
+              if (i < npieces) {
+                const float* ps = slot_ptr(i);
+#pragma unroll
+                for (int r = 0; r < RG; ++r) {
+                  wgt[r] = (rg + r < rows_here) ? ex2(__ldcg(ps + rg + r) - M[r]) : 0.f;
+                  if (rg + r < rows_here) lsum[r] += wgt[r] * __ldcg(ps + p.slot_rows + rg + r);
+                }
+              } else {
+#pragma unroll
+                for (int r = 0; r < RG; ++r) wgt[r] = 0.f;
+              }
+              const int cnt = min(32, npieces - i0);
+#pragma unroll 2
+              for (int j = 0; j < cnt; ++j) {
+                const float* po = slot_ptr(i0 + j) + 2 * p.slot_rows + rg * D;
+                float v[RG][DPL];
+#pragma unroll
+                for (int r = 0; r < RG; ++r)
+#pragma unroll
+                  for (int k = 0; k < DPL; ++k)
+                    v[r][k] = (rg + r < rows_here) ? __ldcg(po + r * D + lane + 32 * k) : 0.f;
+#pragma unroll
+                for (int r = 0; r < RG; ++r) {
+                  const float wr = __shfl_sync(0xffffffffu, wgt[r], j);
+#pragma unroll
+                  for (int k = 0; k < DPL; ++k) acc[r][k] = fmaf(wr, v[r][k], acc[r][k]);
+                }
+              }
+            }
+#pragma unroll
+            for (int r = 0; r < RG; ++r) {
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], o);
+              if (rg + r < rows_here) {
+                const float inv = lsum[r] > 0.f ? 1.f / lsum[r] : 0.f;
+                const int qr = mg * 16 + rg + r;
+                const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+                T* op = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
+                        (long long)t * p.o_st;
+#pragma unroll
+                for (int k = 0; k < DPL; ++k) op[lane + 32 * k] = from_float<T>(acc[r][k] * inv);
+              }
+            }
           }
           if (lane == 0) atomicExch(&p.counters[row_id], 0);
         }

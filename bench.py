@@ -45,14 +45,19 @@ UNIT = "tokens/s"
 FALLBACK_HBM_GBS = 6650.0
 
 
-def _peak_hbm() -> tuple[float, str]:
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def _peaks() -> tuple[float, float, str]:
+    """(HBM GB/s, dense bf16 TFLOP/s burst, source) from MEASURED_PEAKS.json."""
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
         except (KeyError, ValueError):
             pass
-    return FALLBACK_HBM_GBS, "fallback"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -204,6 +209,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the workload's per-GPU batch (smaller cases for ncu captures)")
+    ap.add_argument("--graph", action="store_true",
+                    help="time replays of a CUDA graph holding the step (append + decode) instead of eager calls")
     ap.add_argument("--shard", choices=["auto", "seq", "head"], default="auto",
                     help="multi-GPU layout: sequences (weak scaling) or KV heads + NCCL all-gather "
                          "(strong scaling); auto = heads for cfg5-llama3-70b, sequences otherwise")
@@ -219,7 +226,8 @@ def main() -> None:
 
     from llm_serving_runtime_b200 import paged_attention_decode
     from llm_serving_runtime_b200.sharding import HeadShardedDecode, kv_head_range, shard_sequences
-    from llm_serving_runtime_b200.workloads import SPECS, algorithmic_bytes, make_workload, sample_lengths
+    from llm_serving_runtime_b200.workloads import SPECS, algorithmic_bytes, attention_flops, make_workload, \
+        sample_lengths
 
     world, rank, local = _dist_setup()
     if world != args.gpus:
@@ -249,8 +257,24 @@ def main() -> None:
         gather = None
     B, q = w.batch, w.q_len
     out = torch.empty_like(w.query)
+    graph = None
+    if args.graph:
+        if gather is not None:
+            raise SystemExit("--graph covers the single-rank and sequence-sharded steps")
+        from llm_serving_runtime_b200.cuda_graph import DecodeStepGraph
+
+        graph = DecodeStepGraph([w.key_cache], [w.value_cache], batch=B, max_blocks=w.block_tables.shape[1],
+                                num_q_heads=w.query.shape[1], q_len=q, scale=w.scale)
+        graph.query[0].copy_(w.query)
+        graph.new_key[0].copy_(w.new_key)
+        graph.new_value[0].copy_(w.new_value)
+        graph.block_tables.copy_(w.block_tables)
+        graph.context_lens.copy_(w.context_lens)
+        graph.slot_mapping.copy_(w.slot_mapping)
 
     def step():
+        if graph is not None:
+            return graph.replay()[0]
         if gather is not None:
             return gather(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
                           w.slot_mapping, w.new_key, w.new_value, out=out)
@@ -306,8 +330,14 @@ def main() -> None:
     dec_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
     dec_bytes = algorithmic_bytes(w, include_append=False)
     call_bytes = algorithmic_bytes(w, include_append=True)
-    achieved = dec_bytes / (dec_ms / 1e3) / 1e9
-    peak, peak_src = _peak_hbm()
+    dec_flops = attention_flops(w)
+    peak_hbm, peak_tensor, peak_src = _peaks()
+    # the bound is whichever resource needs more time at its peak
+    tensor_bound = dec_flops / (peak_tensor * 1e12) > dec_bytes / (peak_hbm * 1e9)
+    if tensor_bound:
+        achieved, peak, bound, r_unit = dec_flops / (dec_ms / 1e3) / 1e12, peak_tensor, "tensor", "TFLOP/s"
+    else:
+        achieved, peak, bound, r_unit = dec_bytes / (dec_ms / 1e3) / 1e9, peak_hbm, "hbm", "GB/s"
 
     # ---- end to end through the public API with host buffers ----
     # Every step uploads its own inputs from pinned host memory and downloads its
@@ -393,7 +423,7 @@ def main() -> None:
     if rank != 0:
         return
     ratio = _traffic_ratio_from_profiles(args.workload)
-    traffic = None if ratio is None else ratio * dec_bytes
+    traffic = None if (ratio is None or tensor_bound) else ratio * dec_bytes
     line = {
         "metric": METRIC,
         "value": value,
@@ -414,13 +444,15 @@ def main() -> None:
             "parallelism": (f"kvhead-shard{world}+allgather" if shard == "head" else f"seq-shard{world}")
             if world > 1 else "single",
             "l2": "inputs larger than L2 (no flush)",
+            "launch": "cuda-graph replay" if args.graph else "eager",
             "bytes_per_call": call_bytes,
         },
         "hbm_gbs_per_call": call_bytes / (ms_per_step / 1e3) / 1e9,
         "roofline": {
-            "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "bound": bound, "achieved": achieved, "peak": peak, "unit": r_unit, "frac": achieved / peak,
             "traffic": traffic, "peak_source": peak_src, "kernel": "pa::decode_mma_kernel",
-            "kernel_ms": dec_ms, "algorithmic_bytes": dec_bytes,
+            "kernel_ms": dec_ms, "algorithmic_bytes": dec_bytes, "flops": dec_flops,
+            "hbm_gbs": dec_bytes / (dec_ms / 1e3) / 1e9, "tflops": dec_flops / (dec_ms / 1e3) / 1e12,
         },
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "overlap": "2 copy streams, double-buffered", "result_matches_device_run": ok},

@@ -36,13 +36,24 @@ namespace pa {
 namespace {
 
 struct Cursor {
-  int b;  // sequence
-  int r;  // row within the sequence: kv_head * NMG + m-group
-  int u;  // unit within the row
-  int n;  // units in the row
+  int b;   // sequence
+  int h;   // kv head
+  int mg;  // query-row group (16 rows of the G * q_len rows of this kv head)
+  int u;   // unit within the row
+  int n;   // units in the row
 };
 
 }  // namespace
+
+// Query rows of one kv head are ordered token-major: row qr is query token
+// qr / G of query head h*G + qr % G, so a 16-row group holds consecutive tokens
+// of every head that reads this kv head.  A group whose latest token is t_max
+// attends positions 0 .. L - q_len + t_max: it scans that many 16-token units.
+__device__ __forceinline__ int group_units(int L, int mg, const DecodeParams& p) {
+  const int last_row = min(16 * mg + 15, p.GQ - 1);
+  const int lim = L - p.q_len + last_row / p.G;  // last attendable position
+  return lim < 0 ? 0 : (lim + kUnitTokens) / kUnitTokens;
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
@@ -97,7 +108,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       }
       if (L < 0) L = 0;
       s_lens[b] = L;
-      local += (L + kUnitTokens - 1) / kUnitTokens;
+      int units = 0;
+      for (int mg = 0; mg < p.NMG; ++mg) units += group_units(L, mg, p);
+      local += units * p.Hkv;
     }
     int incl = local;
 #pragma unroll
@@ -111,33 +124,37 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     for (int w = 0; w < warp; ++w) run += s_warp_tot[w];
     for (int b = beg; b < end; ++b) {
       s_pref[b] = run;
-      run += (s_lens[b] + kUnitTokens - 1) / kUnitTokens;
+      int units = 0;
+      for (int mg = 0; mg < p.NMG; ++mg) units += group_units(s_lens[b], mg, p);
+      run += units * p.Hkv;
     }
     if (tid == nthr - 1) s_pref[B] = run;
   }
   fence_mbar_init();
   __syncthreads();
 
-  // Sequences with nothing to attend produce zeros (their rows get no unit).
+  // Row groups with nothing to attend get no unit: their rows are zero.
   for (int b = blockIdx.x; b < B; b += gridDim.x) {
-    if (s_lens[b] != 0) continue;
-    const int rows = p.Hq * p.q_len;
-    for (int i = tid; i < rows * (D / 2); i += blockDim.x) {
-      const int row = i / (D / 2);
-      const int d2 = i - row * (D / 2);
-      const int head = row / p.q_len;
-      const int t = row - head * p.q_len;
-      T* o = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)head * p.o_sh +
-             (long long)t * p.o_st + 2 * d2;
-      *reinterpret_cast<uint32_t*>(o) = 0u;
+    for (int mg = 0; mg < p.NMG; ++mg) {
+      if (group_units(s_lens[b], mg, p) != 0) continue;
+      const int rows = min(16, p.GQ - 16 * mg);
+      for (int i = tid; i < p.Hkv * rows * (D / 2); i += blockDim.x) {
+        const int d2 = i % (D / 2);
+        const int hr = i / (D / 2);
+        const int h = hr / rows;
+        const int qr = 16 * mg + (hr - h * rows);
+        const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
+        T* o = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
+               (long long)t * p.o_st + 2 * d2;
+        *reinterpret_cast<uint32_t*>(o) = 0u;
+      }
     }
   }
 
   // Everything below reads the KV cache, which the previous kernel may write.
   pdl_wait_previous();
 
-  const int rows_per_b = p.Hkv * p.NMG;
-  const long long W = (long long)rows_per_b * s_pref[B];
+  const long long W = s_pref[B];
   if (W == 0) return;
   long long nw_eff = (W + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
   if (nw_eff > p.nw_total) nw_eff = p.nw_total;
@@ -149,33 +166,49 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   if (ws >= we) return;
 
   // Locate the first unit of this warp's slice.
+  // Flat order: sequence, then kv head, then row group, then unit; a sequence
+  // spans Hkv * S_b units with S_b the units of its row groups.
   Cursor start;
   {
     int lo = 0, hi = B - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if ((long long)rows_per_b * s_pref[mid] <= ws)
+      if ((long long)s_pref[mid] <= ws)
         lo = mid;
       else
         hi = mid - 1;
     }
     start.b = lo;
-    start.n = s_pref[lo + 1] - s_pref[lo];
-    const long long off = ws - (long long)rows_per_b * s_pref[lo];
-    start.r = (int)(off / start.n);
-    start.u = (int)(off - (long long)start.r * start.n);
+    const int S = (s_pref[lo + 1] - s_pref[lo]) / p.Hkv;
+    int off = (int)(ws - s_pref[lo]);
+    start.h = off / S;
+    off -= start.h * S;
+    const int L = s_lens[lo];
+    start.mg = 0;
+    while (true) {
+      const int n = group_units(L, start.mg, p);
+      if (off < n) {
+        start.n = n;
+        break;
+      }
+      off -= n;
+      ++start.mg;
+    }
+    start.u = off;
   }
   auto advance = [&](Cursor& c) {
-    if (++c.u == c.n) {
-      c.u = 0;
-      if (++c.r == rows_per_b) {
-        c.r = 0;
-        do {
-          ++c.b;
-        } while (c.b < B && s_pref[c.b + 1] == s_pref[c.b]);
-        if (c.b < B) c.n = s_pref[c.b + 1] - s_pref[c.b];
+    if (++c.u < c.n) return;
+    c.u = 0;
+    do {
+      if (++c.mg == p.NMG) {
+        c.mg = 0;
+        if (++c.h == p.Hkv) {
+          c.h = 0;
+          if (++c.b >= B) return;
+        }
       }
-    }
+      c.n = group_units(s_lens[c.b], c.mg, p);
+    } while (c.n == 0);
   };
 
   const uint32_t my_ring = ring_addr + (uint32_t)(warp * stages) * STAGE_BYTES;
@@ -199,7 +232,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   };
 
   auto issue = [&](int slot) {
-    const int h = pc.r / p.NMG;
+    const int h = pc.h;
     const uint32_t stage = my_ring + (uint32_t)slot * STAGE_BYTES;
     const uint32_t bar = my_bars + (uint32_t)slot * 8u;
     const int tok0 = pc.u * kUnitTokens;
@@ -265,18 +298,20 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   float o_acc[NDT][4];
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   int lim0 = 0, lim1 = 0;  // last attendable token of rows qrow0 / qrow0 + 8
+  int mask_from = 0;       // units ending past this position need the causal mask
   bool piece_first = true, piece_from_row_start = false;
 
   while (cf < we) {
     const int b = cc.b;
-    const int h = cc.r / p.NMG;
-    const int mg = cc.r - h * p.NMG;
+    const int h = cc.h;
+    const int mg = cc.mg;
     const int L = s_lens[b];
 
     if (cc.u == 0 || cf == ws) {
       // Begin a piece: load the packed query tile of (b, h, m-group) as A fragments.
       piece_first = (cf == ws);
       piece_from_row_start = (cc.u == 0);
+      mask_from = L - p.q_len + (16 * mg) / p.G;  // the group's earliest row's limit
       const int qr0 = mg * 16 + qrow0;
       const int qr1 = qr0 + 8;
       const T* qp0 = nullptr;
@@ -284,13 +319,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       lim0 = L - 1;
       lim1 = L - 1;
       if (qr0 < p.GQ) {
-        const int g = qr0 / p.q_len, t = qr0 - (qr0 / p.q_len) * p.q_len;
+        const int t = qr0 / p.G, g = qr0 - (qr0 / p.G) * p.G;
         qp0 = static_cast<const T*>(p.q) + (long long)b * p.q_sb +
               (long long)(h * p.G + g) * p.q_sh + (long long)t * p.q_st;
         lim0 = L - p.q_len + t;
       }
       if (qr1 < p.GQ) {
-        const int g = qr1 / p.q_len, t = qr1 - (qr1 / p.q_len) * p.q_len;
+        const int t = qr1 / p.G, g = qr1 - (qr1 / p.G) * p.G;
         qp1 = static_cast<const T*>(p.q) + (long long)b * p.q_sb +
               (long long)(h * p.G + g) * p.q_sh + (long long)t * p.q_st;
         lim1 = L - p.q_len + t;
@@ -351,7 +386,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) x[n][i] = s_acc[n][i] * p.scale_log2;
-    if (tok_base + kUnitTokens - 1 > L - p.q_len) {
+    if (tok_base + kUnitTokens - 1 > mask_from) {
 #pragma unroll
       for (int n = 0; n < 2; ++n)
 #pragma unroll
@@ -452,13 +487,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         T* op1 = nullptr;
         if (r0_ok) {
           const int qr = mg * 16 + qrow0;
-          const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+          const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
           op0 = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
                 (long long)t * p.o_st;
         }
         if (r1_ok) {
           const int qr = mg * 16 + qrow0 + 8;
-          const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+          const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
           op1 = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
                 (long long)t * p.o_st;
         }
@@ -583,7 +618,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
               if (rg + r < rows_here) {
                 const float inv = lsum[r] > 0.f ? 1.f / lsum[r] : 0.f;
                 const int qr = mg * 16 + rg + r;
-                const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
+                const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
                 T* op = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
                         (long long)t * p.o_st;
 #pragma unroll

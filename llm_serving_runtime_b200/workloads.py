@@ -29,6 +29,7 @@ __all__ = [
     "make_workload",
     "sample_lengths",
     "algorithmic_bytes",
+    "attention_flops",
     "lpt_partition",
 ]
 
@@ -71,6 +72,10 @@ SPECS: dict[str, WorkloadSpec] = {
     # Llama-3-70B shape, bf16
     "cfg5-llama3-70b": WorkloadSpec("cfg5-llama3-70b", 512, 64, 8, 128, 16, torch.bfloat16, 1,
                                     "uniform", 2048, 16384, 0.5, pool_slack=0.0, seed=1005),
+    # chunked prefill over paged KV (next to the path): 512 new tokens per
+    # sequence on top of 0..4096 cached ones, Llama-3-8B heads
+    "prefill-llama3-8b": WorkloadSpec("prefill-llama3-8b", 16, 32, 8, 128, 16, torch.bfloat16, 512,
+                                      "uniform", 0, 4096, 0.5, seed=1006),
 }
 
 
@@ -255,6 +260,16 @@ def make_workload(
         unique_blocks=unique,
         extra={"kv_heads": (h0, Hkv)},
     )
+
+
+def attention_flops(w: DecodeWorkload) -> int:
+    """Multiply-add FLOPs of QK^T and PV over the attended (causal) positions:
+    4 * D * sum over query rows of the positions each attends."""
+    B, Hq, q, D = w.query.shape
+    L = w.attended_lengths()
+    t = torch.arange(q)
+    per_row = (L[:, None] - q + t[None, :] + 1).clamp_min(0)  # positions row (b, t) attends
+    return int(4 * D * Hq * per_row.sum().item())
 
 
 def algorithmic_bytes(w: DecodeWorkload, *, include_append: bool = True, unique: bool = False) -> int:

@@ -1,0 +1,50 @@
+"""Multi-query attention over paged KV (chunked prefill / long speculative
+verify): q_len new tokens per sequence, causal over them, on top of the cached
+context — the same op as decode.  Checked against the oracle, which restates
+the reference's eager masked attention (block_paged_attention.py:50-59)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from _util import excess_err, max_err
+from llm_serving_runtime_b200 import paged_attention_decode
+from llm_serving_runtime_b200.workloads import make_workload
+from oracle import oracle
+from test_decode_gpu import _synthetic
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+CASES = [
+    # (B, Hq, Hkv, D, bs, dtype, context_lens, q_len)
+    (3, 32, 8, 128, 16, torch.bfloat16, [0, 100, 1000], 64),
+    (2, 32, 8, 128, 16, torch.bfloat16, [0, 0], 512),        # pure prefill, nothing cached
+    (3, 14, 2, 64, 16, torch.float16, [5, 300, 2000], 128),
+    (2, 64, 8, 128, 16, torch.bfloat16, [17, 700], 33),       # G = 8, ragged chunk
+    (2, 28, 4, 128, 16, torch.bfloat16, [3, 64], 16),          # G = 7
+    (2, 8, 8, 64, 32, torch.float16, [40, 1], 100),            # MHA, block size 32
+    (2, 8, 2, 128, 8, torch.bfloat16, [9, 250], 40),           # block size 8
+    (2, 8, 2, 64, 16, torch.float32, [30, 200], 48),           # fp32 path
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,bs,dtype,lens,q_len", CASES)
+def test_multi_query_chunks_vs_oracle(B, Hq, Hkv, D, bs, dtype, lens, q_len):
+    q, kc, vc, bt, cl = _synthetic(B, Hq, Hkv, D, bs, dtype, lens, q_len, seed=q_len + D)
+    out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), D ** -0.5,
+                                 validate=True)
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, D ** -0.5)
+    assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"
+
+
+def test_prefill_workload_with_append_sampled_rows():
+    from _util import oracle_rows
+
+    w = make_workload("prefill-llama3-8b", device=DEV)
+    out = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                                 w.slot_mapping, w.new_key, w.new_value, validate=True)
+    rows = [0, 5, 11]
+    ref = oracle_rows(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale, w.q_len, rows)
+    assert excess_err(out[rows], ref) <= 0, f"max abs err {max_err(out[rows], ref)}"

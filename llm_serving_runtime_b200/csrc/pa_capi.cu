@@ -378,6 +378,15 @@ int pa_decode(const pa_decode_args* a, void* stream) {
       info->prepared_smem[di][dj] = smem;
     }
   }
+  // Many query rows per KV head (chunked prefill, long verify) with enough
+  // 128-row tiles to fill the GPU: the multi-query kernel shares each K/V tile
+  // across 128 rows.  Otherwise the split-K decode kernel.
+  const long long prefill_tiles = (long long)p.B * p.Hkv * ((p.GQ + 127) / 128);
+  if (p.GQ >= 64 && prefill_tiles >= info->num_sms) {
+    e = pa::launch_prefill_mma(p, tmk, tmv, dtype, pdl, strm);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+    return PA_OK;
+  }
   e = pa::launch_decode_mma(p, tmk, tmv, dtype, grid, smem, pdl, strm);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return PA_OK;

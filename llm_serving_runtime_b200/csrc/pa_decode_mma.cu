@@ -30,6 +30,7 @@
 
 #include "pa_common.cuh"
 #include "pa_internal.h"
+#include "pa_tile_math.cuh"
 
 namespace pa {
 
@@ -330,14 +331,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
               (long long)(h * p.G + g) * p.q_sh + (long long)t * p.q_st;
         lim1 = L - p.q_len + t;
       }
-#pragma unroll
-      for (int ks = 0; ks < KSTEPS; ++ks) {
-        const int d = ks * 16 + 2 * quad;
-        qa[ks][0] = qp0 ? __ldg(reinterpret_cast<const unsigned int*>(qp0 + d)) : 0u;
-        qa[ks][1] = qp1 ? __ldg(reinterpret_cast<const unsigned int*>(qp1 + d)) : 0u;
-        qa[ks][2] = qp0 ? __ldg(reinterpret_cast<const unsigned int*>(qp0 + d + 8)) : 0u;
-        qa[ks][3] = qp1 ? __ldg(reinterpret_cast<const unsigned int*>(qp1 + d + 8)) : 0u;
-      }
+      load_query_frags<T, D>(qa, qp0, qp1, quad);
 #pragma unroll
       for (int nd = 0; nd < NDT; ++nd) {
         o_acc[nd][0] = o_acc[nd][1] = o_acc[nd][2] = o_acc[nd][3] = 0.f;
@@ -363,102 +357,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     const uint32_t kbase = my_ring + (uint32_t)slot * STAGE_BYTES;
     const uint32_t vbase = kbase + TILE_BYTES;
 
-    // ---- S = Q K^T (16 query rows x 16 tokens), fp32 accumulate ----
-    float s_acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    {
-      const int tok = ((lane >> 4) << 3) | (lane & 7);
-#pragma unroll
-      for (int ks = 0; ks < KSTEPS; ++ks) {
-        const int chunk = 2 * ks + ((lane >> 3) & 1);
-        const uint32_t addr = kbase + (uint32_t)(chunk >> 3) * 2048u + (uint32_t)tok * 128u +
-                              ((uint32_t)((chunk & 7) ^ (tok & 7)) << 4);
-        uint32_t k0, k1, k2, k3;
-        ldsm_x4(addr, k0, k1, k2, k3);
-        Mma16816<T>::run(s_acc[0], qa[ks], k0, k1);
-        Mma16816<T>::run(s_acc[1], qa[ks], k2, k3);
-      }
-    }
-
-    // ---- scale, mask, online softmax ----
-    const int tok_base = cc.u * kUnitTokens;
-    float x[2][4];
-#pragma unroll
-    for (int n = 0; n < 2; ++n)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) x[n][i] = s_acc[n][i] * p.scale_log2;
-    if (tok_base + kUnitTokens - 1 > mask_from) {
-#pragma unroll
-      for (int n = 0; n < 2; ++n)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int tok = tok_base + n * 8 + 2 * quad + (i & 1);
-          const int lim = (i < 2) ? lim0 : lim1;
-          if (tok > lim) x[n][i] = -INFINITY;
-        }
-    }
-    float mx0 = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
-    float mx1 = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0);
-    const float mn1 = fmaxf(m1, mx1);
-    const float base0 = (mn0 == -INFINITY) ? 0.f : mn0;
-    const float base1 = (mn1 == -INFINITY) ? 0.f : mn1;
-    const float alpha0 = ex2(m0 - base0);
-    const float alpha1 = ex2(m1 - base1);
-    float pr[2][4];
-#pragma unroll
-    for (int n = 0; n < 2; ++n) {
-      pr[n][0] = ex2(x[n][0] - base0);
-      pr[n][1] = ex2(x[n][1] - base0);
-      pr[n][2] = ex2(x[n][2] - base1);
-      pr[n][3] = ex2(x[n][3] - base1);
-    }
-    l0 = l0 * alpha0 + (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
-    l1 = l1 * alpha1 + (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
-    m0 = mn0;
-    m1 = mn1;
-#pragma unroll
-    for (int nd = 0; nd < NDT; ++nd) {
-      o_acc[nd][0] *= alpha0;
-      o_acc[nd][1] *= alpha0;
-      o_acc[nd][2] *= alpha1;
-      o_acc[nd][3] *= alpha1;
-    }
-    uint32_t pa[4];
-    pa[0] = pack2<T>(pr[0][0], pr[0][1]);
-    pa[1] = pack2<T>(pr[0][2], pr[0][3]);
-    pa[2] = pack2<T>(pr[1][0], pr[1][1]);
-    pa[3] = pack2<T>(pr[1][2], pr[1][3]);
-
-    // ---- O += P V ----
-    {
-      // Tokens at or past L hold whatever the cache had there; zero them so a
-      // non-finite stale value cannot turn 0 * v into NaN.
-      uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
-      if (tok_base + kUnitTokens > L) {
-        const int t0 = tok_base + 2 * quad;
-        vm0 = (t0 < L ? 0x0000ffffu : 0u) | (t0 + 1 < L ? 0xffff0000u : 0u);
-        vm1 = (t0 + 8 < L ? 0x0000ffffu : 0u) | (t0 + 9 < L ? 0xffff0000u : 0u);
-      }
-      const int tok = (((lane >> 3) & 1) << 3) | (lane & 7);
-#pragma unroll
-      for (int nd = 0; nd < NDT; nd += 2) {
-        const int chunk = nd + (lane >> 4);
-        const uint32_t addr = vbase + (uint32_t)(chunk >> 3) * 2048u + (uint32_t)tok * 128u +
-                              ((uint32_t)((chunk & 7) ^ (tok & 7)) << 4);
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4_trans(addr, v0, v1, v2, v3);
-        v0 &= vm0;
-        v1 &= vm1;
-        v2 &= vm0;
-        v3 &= vm1;
-        Mma16816<T>::run(o_acc[nd], pa, v0, v1);
-        Mma16816<T>::run(o_acc[nd + 1], pa, v2, v3);
-      }
-    }
+    // ---- QK^T, masked online softmax, PV on tensor cores ----
+    attend_unit<T, D>(kbase, vbase, qa, o_acc, m0, m1, l0, l1, cc.u * kUnitTokens, L, lim0, lim1, mask_from,
+                      p.scale_log2, lane);
 
     // ---- refill this slot with the unit `stages` ahead ----
     __syncwarp();
@@ -481,8 +382,6 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       const bool r1_ok = qrow0 + 8 < rows_here;
       if (row_end && piece_from_row_start) {
         // The whole row is in this piece: normalise and store.
-        const float inv0 = lt0 > 0.f ? 1.f / lt0 : 0.f;
-        const float inv1 = lt1 > 0.f ? 1.f / lt1 : 0.f;
         T* op0 = nullptr;
         T* op1 = nullptr;
         if (r0_ok) {
@@ -497,16 +396,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           op1 = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
                 (long long)t * p.o_st;
         }
-#pragma unroll
-        for (int nd = 0; nd < NDT; ++nd) {
-          const int d = nd * 8 + 2 * quad;
-          if (op0)
-            *reinterpret_cast<uint32_t*>(op0 + d) =
-                pack2<T>(o_acc[nd][0] * inv0, o_acc[nd][1] * inv0);
-          if (op1)
-            *reinterpret_cast<uint32_t*>(op1 + d) =
-                pack2<T>(o_acc[nd][2] * inv1, o_acc[nd][3] * inv1);
-        }
+        store_rows<T, D>(op0, op1, o_acc, lt0, lt1, quad);
       } else {
         // Partial: (m, l, acc) to this warp's slot, then count the arrival.
         const int slot_idx = 2 * gw + (piece_first ? 0 : 1);

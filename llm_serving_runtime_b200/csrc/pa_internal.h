@@ -14,6 +14,10 @@ namespace pa {
 // Warps per CTA of the tensor-core decode kernel.  Each warp is a self-fed
 // engine with its own ring of shared-memory stages.
 constexpr int kDecodeWarps = 8;
+// Multi-query (prefill) kernel: 8 consumer warps (128 query rows) + 1 producer.
+constexpr int kPrefillWarps = 8;
+constexpr int kPrefillThreads = (kPrefillWarps + 1) * 32;
+constexpr int kPrefillStages = 6;
 // Minimum number of 16-token units a warp's share of the flat work list holds
 // before the kernel stops splitting the work further.
 constexpr int kMinUnitsPerWarp = 8;
@@ -80,6 +84,8 @@ cudaError_t launch_kv_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
                               int dtype, int grid, size_t smem, bool pdl, cudaStream_t stream);
 cudaError_t launch_decode_f32(const DecodeParams& p, bool pdl, cudaStream_t stream);
+cudaError_t launch_prefill_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
+                               bool pdl, cudaStream_t stream);
 
 // Shared-memory bytes of the tensor-core kernel for given stage count.
 size_t decode_mma_smem_bytes(int D, int B, int stages);

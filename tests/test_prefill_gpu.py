@@ -27,6 +27,11 @@ CASES = [
     (2, 8, 8, 64, 32, torch.float16, [40, 1], 100),            # MHA, block size 32
     (2, 8, 2, 128, 8, torch.bfloat16, [9, 250], 40),           # block size 8
     (2, 8, 2, 64, 16, torch.float32, [30, 200], 48),           # fp32 path
+    # enough 128-row tiles (>= one per SM) to take the multi-query kernel:
+    (10, 32, 8, 128, 16, torch.bfloat16, [0, 50, 300, 1000, 17, 0, 2000, 64, 5, 700], 256),
+    (12, 14, 2, 64, 16, torch.float16, [1, 2, 3, 900, 100, 0, 33, 64, 65, 500, 8, 1200], 640),
+    (6, 32, 8, 128, 8, torch.bfloat16, [3, 40, 0, 600, 129, 255], 200),   # block size 8
+    (8, 64, 8, 128, 32, torch.bfloat16, [16, 0, 400, 31, 1000, 7, 65, 300], 96),  # G = 8, bs 32
 ]
 
 

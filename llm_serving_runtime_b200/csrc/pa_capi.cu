@@ -7,6 +7,7 @@
 #include <cudaTypedefs.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -112,6 +113,18 @@ int encode_cache_map(CUtensorMap* map, const pa_cache_view& v, int dtype, int D,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(PA_ERR_UNSUPPORTED, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
   return PA_OK;
+}
+
+// Kernel choice for multi-query tiles: PA_B200_MULTIQUERY=mma forces the
+// mma.sync kernel (comparison / fallback); default is the tcgen05 kernel.
+constexpr int kPolicyAuto = 0, kPolicyMma = 1;
+int multiquery_policy() {
+  static int policy = -1;
+  if (policy < 0) {
+    const char* v = getenv("PA_B200_MULTIQUERY");
+    policy = (v != nullptr && strcmp(v, "mma") == 0) ? kPolicyMma : kPolicyAuto;
+  }
+  return policy;
 }
 
 struct DecodeShape {
@@ -383,8 +396,17 @@ int pa_decode(const pa_decode_args* a, void* stream) {
   // across 128 rows.  Otherwise the split-K decode kernel.
   const long long prefill_tiles = (long long)p.B * p.Hkv * ((p.GQ + 127) / 128);
   if (p.GQ >= 64 && prefill_tiles >= info->num_sms) {
-    e = pa::launch_prefill_mma(p, tmk, tmv, dtype, pdl, strm);
-    if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+    // tcgen05 kernel: each thread moves its query / output row in 16-byte pieces.
+    const bool rows16 = aligned_ptr(a->query, 16) && aligned_ptr(a->out, 16) &&
+                        ((a->query_stride_b | a->query_stride_h | a->query_stride_t | a->out_stride_b |
+                          a->out_stride_h | a->out_stride_t) & 7) == 0;
+    if (rows16 && multiquery_policy() != kPolicyMma) {
+      e = pa::launch_prefill_umma(p, tmk, tmv, dtype, pdl, strm);
+      if (e != cudaSuccess) return cuda_fail(e, "tcgen05 multi-query launch");
+    } else {
+      e = pa::launch_prefill_mma(p, tmk, tmv, dtype, pdl, strm);
+      if (e != cudaSuccess) return cuda_fail(e, "multi-query launch");
+    }
     return PA_OK;
   }
   e = pa::launch_decode_mma(p, tmk, tmv, dtype, grid, smem, pdl, strm);

@@ -18,6 +18,8 @@ constexpr int kDecodeWarps = 8;
 constexpr int kPrefillWarps = 8;
 constexpr int kPrefillThreads = (kPrefillWarps + 1) * 32;
 constexpr int kPrefillStages = 6;
+// tcgen05 multi-query kernel: 4 softmax warps + 1 TMA producer + 1 MMA-issue warp.
+constexpr int kUmmaThreads = 6 * 32;
 // Minimum number of 16-token units a warp's share of the flat work list holds
 // before the kernel stops splitting the work further.
 constexpr int kMinUnitsPerWarp = 8;
@@ -86,6 +88,8 @@ cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& tmk, con
 cudaError_t launch_decode_f32(const DecodeParams& p, bool pdl, cudaStream_t stream);
 cudaError_t launch_prefill_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
                                bool pdl, cudaStream_t stream);
+cudaError_t launch_prefill_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
+                                bool pdl, cudaStream_t stream);
 
 // Shared-memory bytes of the tensor-core kernel for given stage count.
 size_t decode_mma_smem_bytes(int D, int B, int stages);

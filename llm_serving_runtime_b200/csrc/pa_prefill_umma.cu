@@ -1,0 +1,548 @@
+// pa_prefill_umma.cu — multi-query attention over paged KV on 5th-generation
+// tensor cores (tcgen05 / UMMA, accumulators in TMEM), fp16 / bf16, sm_100a.
+//
+// Same contract and row layout as the other decode kernels: rows of one KV head
+// are token-major (row r = query token r / G of head h*G + r % G); query token t
+// attends positions 0 .. L - q_len + t.  A CTA owns a 128-row tile of one
+// (sequence, kv head) and streams the sequence's K/V in 64-token chunks:
+//
+//   warp 4 (producer)  TMA-loads each chunk's four 16-token units (K and V, two
+//                      64-column halves each, 128-byte swizzle) into a 3-stage ring;
+//   warp 5 (MMA)       one thread issues S = Q K^T (M=128, N=64, K=D) into a
+//                      double-buffered TMEM S, and O += P V (M=128, N=D, K=64)
+//                      into TMEM O, signalling mbarriers with tcgen05.commit;
+//   warps 0-3 (softmax) thread i owns query row i = TMEM lane i: it loads its S
+//                      row (tcgen05.ld), masks, takes the max and exponentials
+//                      without any cross-thread reduction, writes its P row
+//                      (bf16: hi and lo parts, so P.V keeps ~16 bits of P) into
+//                      swizzled shared memory as the A operand of the PV MMA,
+//                      and finally reads O back, normalises and stores it.
+//
+// The online softmax keeps a reference max per row and rescales O (TMEM load,
+// scale, store) only when a chunk raises the row max by more than 2^8, so p
+// stays below 256 and the arithmetic is exact; most chunks skip the rescale.
+// Every wait is bounded; TMEM is always released before the CTA exits.
+#include <math.h>
+
+#include "pa_common.cuh"
+#include "pa_internal.h"
+#include "pa_tile_math.cuh"
+
+namespace pa {
+
+namespace {
+
+constexpr int kChunk = 64;             // tokens per chunk (N of the QK^T MMA)
+constexpr int kUmmaStages = 3;         // K/V chunks in flight
+constexpr uint32_t kTmemCols = 256;    // S double buffer (2 x 64) + O (<= 128)
+constexpr float kRescaleThreshold = 8.f;  // log2 units: rescale when the max grows by > 2^8
+
+// UMMA A/B element format code of kind::f16: 0 = fp16, 1 = bf16.
+template <typename T>
+struct kUmmaFormat;
+template <>
+struct kUmmaFormat<__half> {
+  static constexpr uint32_t value = 0;
+};
+template <>
+struct kUmmaFormat<__nv_bfloat16> {
+  static constexpr uint32_t value = 1;
+};
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;  // 128-byte swizzle
+  return d;
+}
+
+// kind::f16 instruction descriptor: D fp32, A/B fp16 (fmt 0) or bf16 (fmt 1).
+__device__ __forceinline__ uint32_t umma_idesc(int M, int N, uint32_t ab_fmt, int b_mn_major) {
+  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((uint32_t)(b_mn_major & 1) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled region.
+__device__ __forceinline__ uint32_t sw128_chunk(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+}  // namespace
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kUmmaThreads, 1)
+    prefill_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                        const DecodeParams p) {
+  constexpr int HALVES = D / 64;
+  constexpr uint32_t HALF_BYTES = kChunk * 128;          // 64 rows x 128 B
+  constexpr uint32_t KV_BYTES = 2 * HALVES * HALF_BYTES;  // K and V of one chunk
+  constexpr uint32_t Q_BYTES = HALVES * 128 * 128;        // 128 rows x D
+  constexpr uint32_t P_BYTES = 128 * 128;                 // 128 rows x 64 tokens (16-bit)
+  constexpr bool kSplit = kSplitProbabilities<T>::value;
+  constexpr uint32_t FMT = kUmmaFormat<T>::value;
+  const int S = kUmmaStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint8_t* s_kv = smem;                                 // [stage][K halves | V halves]
+  uint8_t* s_q = s_kv + S * KV_BYTES;                   // [halves][128 rows x 128 B]
+  uint8_t* s_p = s_q + Q_BYTES;                         // [buffer 0/1][hi | lo] 16 KB each
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_p + 4 * P_BYTES);
+  uint64_t* kv_full = bars;                             // [S]
+  uint64_t* kv_empty = kv_full + S;                     // [S]
+  uint64_t* s_full = kv_empty + S;                      // [2]
+  uint64_t* s_free = s_full + 2;                        // [2]
+  uint64_t* p_full = s_free + 2;                        // [2]
+  uint64_t* pv_done = p_full + 2;                       // [2]
+  uint64_t* q_ready = pv_done + 2;                      // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int BH = p.B * p.Hkv;
+  const int MT = (p.GQ + 127) / 128;
+  const int mt = MT - 1 - (int)(blockIdx.x / BH);  // latest (heaviest) tiles first
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / p.Hkv;
+  const int h = bh - b * p.Hkv;
+
+  int L = p.context_lens[b] + p.len_offset;
+  const int cap = p.max_blocks * p.bs;
+  if (L > cap) {
+    if (tid == 0 && h == 0 && mt == MT - 1) raise_flag(p.status, PA_DEVERR_TABLE_UNDERRUN);
+    L = cap;
+  }
+  if (L < 0) L = 0;
+  const int row0 = mt * 128;
+  const int rows_tile = min(128, p.GQ - row0);
+  const int lim_tile = L - p.q_len + (row0 + rows_tile - 1) / p.G;
+  const int n_chunks = lim_tile < 0 ? 0 : (lim_tile + kChunk) / kChunk;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_addr(&kv_full[s]), 1);
+      mbar_init(smem_addr(&kv_empty[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&s_full[i]), 1);
+      mbar_init(smem_addr(&s_free[i]), 4);
+      mbar_init(smem_addr(&p_full[i]), 4);
+      mbar_init(smem_addr(&pv_done[i]), 1);
+    }
+    mbar_init(smem_addr(q_ready), 4);
+    prefetch_tensormap(&tmk);
+    prefetch_tensormap(&tmv);
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_mbar_init();
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_s0 = tmem;        // columns 0..63 / 64..127: S buffers
+  const uint32_t tmem_o = tmem + 128;   // columns 128 .. 128 + D - 1: O
+  pdl_wait_previous();
+
+  if (warp == 4) {
+    // ---------------- producer: K/V chunks by TMA ----------------
+    int win_base = -1, win_val = -1;
+    const int bs = p.bs;
+    bool ok = true;
+    for (int j = 0; j < n_chunks && ok; ++j) {
+      const int stage = j % S;
+      if (j >= S) {
+        int w = 1;
+        if (lane == 0) w = mbar_wait_bounded(smem_addr(&kv_empty[stage]), (uint32_t)(((j / S) - 1) & 1)) ? 1 : 0;
+        w = __shfl_sync(0xffffffffu, w, 0);
+        if (!w) {
+          if (lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+      const uint32_t base = smem_addr(s_kv + stage * KV_BYTES);
+      const uint32_t bar = smem_addr(&kv_full[stage]);
+      // units of this chunk the sequence reaches
+      const int units = min(4, (L - j * kChunk + 15) / 16);
+      uint32_t tx = 0;
+      int physs[4][2];
+      for (int u = 0; u < 4; ++u) {
+        const int tok0 = j * kChunk + u * 16;
+        const int lb0 = tok0 / bs;
+        const int need = bs >= 16 ? 1 : 16 / bs;
+        if (win_base < 0 || lb0 < win_base || lb0 + need > win_base + 32) {
+          win_base = lb0;
+          const int e = lb0 + lane;
+          win_val = (e < p.max_blocks) ? __ldg(&p.block_tables[(long long)b * p.bt_stride + e]) : -1;
+        }
+        physs[u][0] = __shfl_sync(0xffffffffu, win_val, lb0 - win_base);
+        physs[u][1] = __shfl_sync(0xffffffffu, win_val, (lb0 + 1 - win_base) & 31);
+      }
+      if (lane == 0) {
+        for (int u = 0; u < units; ++u) {
+          const int tok0 = j * kChunk + u * 16;
+          if (bs >= 16) {
+            tx += 2u * HALVES * 2048u;
+          } else {
+            const bool need1 = (tok0 / bs + 1) * bs < L;
+            tx += (need1 ? 2u : 1u) * 2u * HALVES * (uint32_t)bs * 128u;
+          }
+        }
+        mbar_arrive_expect_tx(bar, tx);
+        for (int u = 0; u < units; ++u) {
+          const int tok0 = j * kChunk + u * 16;
+          const int lb0 = tok0 / bs;
+          if (bs >= 16) {
+            const int phys = physs[u][0];
+            const int y = tok0 - lb0 * bs;
+            if (phys < 0 || phys >= p.num_blocks) raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
+#pragma unroll
+            for (int hf = 0; hf < HALVES; ++hf) {
+              tma_load_4d(base + hf * HALF_BYTES + u * 2048u, &tmk, bar, hf * 64, y, h, phys);
+              tma_load_4d(base + (HALVES + hf) * HALF_BYTES + u * 2048u, &tmv, bar, hf * 64, y, h, phys);
+            }
+          } else {
+            const bool need1 = (lb0 + 1) * bs < L;
+            const uint32_t box = (uint32_t)bs * 128u;
+            for (int jj = 0; jj < (need1 ? 2 : 1); ++jj) {
+              const int phys = physs[u][jj];
+              if (phys < 0 || phys >= p.num_blocks) raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
+#pragma unroll
+              for (int hf = 0; hf < HALVES; ++hf) {
+                tma_load_4d(base + hf * HALF_BYTES + u * 2048u + jj * box, &tmk, bar, hf * 64, 0, h, phys);
+                tma_load_4d(base + (HALVES + hf) * HALF_BYTES + u * 2048u + jj * box, &tmv, bar, hf * 64, 0, h,
+                            phys);
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issue (one thread) ----------------
+    if (lane == 0 && n_chunks > 0) {
+      bool ok = mbar_wait_bounded(smem_addr(q_ready), 0);
+      const uint32_t id_s = umma_idesc(128, kChunk, FMT, 0);
+      const uint32_t id_o = umma_idesc(128, D, FMT, 1);
+      const uint32_t q_base = smem_addr(s_q);
+      auto issue_pv = [&](int jp) {
+        const int pb = jp & 1;
+        const uint32_t v_base = smem_addr(s_kv + (jp % S) * KV_BYTES) + HALVES * HALF_BYTES;
+        const uint32_t p_hi = smem_addr(s_p + (2 * pb) * P_BYTES);
+        const uint32_t p_lo = smem_addr(s_p + (2 * pb + 1) * P_BYTES);
+        tmem_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kChunk / 16; ++ks) {
+          const uint64_t vd = umma_desc(v_base + ks * 2048u, HALF_BYTES, 1024);
+          umma_f16(tmem_o, umma_desc(p_hi + ks * 32u, 16, 1024), vd, id_o, (jp > 0 || ks > 0) ? 1u : 0u);
+          if (kSplit) umma_f16(tmem_o, umma_desc(p_lo + ks * 32u, 16, 1024), vd, id_o, 1u);
+        }
+        umma_commit(smem_addr(&pv_done[pb]));
+        umma_commit(smem_addr(&kv_empty[jp % S]));
+      };
+      auto issue_qk = [&](int jq) -> bool {
+        const int stage = jq % S;
+        const int sb = jq & 1;
+        if (!mbar_wait_bounded(smem_addr(&kv_full[stage]), (uint32_t)((jq / S) & 1))) return false;
+        if (jq >= 2 && !mbar_wait_bounded(smem_addr(&s_free[sb]), (uint32_t)(((jq >> 1) - 1) & 1))) return false;
+        tmem_fence_after();
+        const uint32_t k_base = smem_addr(s_kv + stage * KV_BYTES);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t hoff = (uint32_t)(ks >> 2);
+          const uint32_t koff = (uint32_t)(ks & 3) * 32u;
+          umma_f16(tmem_s0 + sb * kChunk, umma_desc(q_base + hoff * 16384u + koff, 16, 1024),
+                   umma_desc(k_base + hoff * HALF_BYTES + koff, 16, 1024), id_s, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(smem_addr(&s_full[sb]));
+        return true;
+      };
+      // QK^T runs one chunk ahead of PV, so the softmax of chunk j+1 can start
+      // as soon as that of chunk j ends.
+      if (ok) ok = issue_qk(0);
+      for (int j = 0; j < n_chunks && ok; ++j) {
+        if (j + 1 < n_chunks) {
+          ok = issue_qk(j + 1);
+          if (!ok) break;
+        }
+        ok = mbar_wait_bounded(smem_addr(&p_full[j & 1]), (uint32_t)((j >> 1) & 1));
+        if (!ok) break;
+        issue_pv(j);
+      }
+      if (!ok) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax warps: thread = query row = TMEM lane ----------------
+    const int r = tid;  // 0..127
+    const int qr = row0 + r;
+    const bool row_ok = qr < p.GQ;
+    int t = 0, g = 0;
+    if (row_ok) {
+      t = qr / p.G;
+      g = qr - t * p.G;
+    }
+    const int lim = row_ok ? L - p.q_len + t : -1;  // last attendable position
+    // Q row -> swizzled K-major tile (row r)
+    {
+      const T* qrow = static_cast<const T*>(p.q) + (long long)b * p.q_sb + (long long)(h * p.G + g) * p.q_sh +
+                      (long long)t * p.q_st;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (row_ok) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
+        *reinterpret_cast<uint4*>(s_q + (c >> 3) * 16384 + sw128_chunk(r, c & 7)) = v;
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_addr(q_ready));
+
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    float m_ref = -INFINITY;  // reference max (log2 domain) of this row
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_chunks; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait_bounded(smem_addr(&s_full[sb]), (uint32_t)((j >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      tmem_fence_after();
+      float x[kChunk];  // raw scores q.k of this row's 64 tokens
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tmem_s0 + sb * kChunk + lane_base, r0);
+        tmem_ld32(tmem_s0 + sb * kChunk + 32 + lane_base, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          x[i] = __uint_as_float(r0[i]);
+          x[32 + i] = __uint_as_float(r1[i]);
+        }
+      }
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&s_free[sb]));
+
+      const int tok0 = j * kChunk;
+      if (tok0 + kChunk - 1 > lim) {  // causal / end-of-sequence mask in this chunk
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i)
+          if (tok0 + i > lim) x[i] = -INFINITY;
+      }
+      float mx_raw = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) mx_raw = fmaxf(mx_raw, x[i]);
+      const float sl2 = p.scale_log2;  // > 0, so max(x * s) = s * max(x)
+      const float mx = mx_raw * sl2;
+      // reference max: move it (and rescale O) only when the row max grows a lot
+      float alpha = 1.f;
+      bool move = false;
+      if (mx > m_ref + kRescaleThreshold || (m_ref == -INFINITY && mx != -INFINITY)) {
+        alpha = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - mx);
+        m_ref = mx;
+        move = true;
+      }
+      const float nbase = (m_ref == -INFINITY) ? 0.f : -m_ref;
+      float ps = 0.f;
+      uint32_t phi[kChunk / 2], plo[kChunk / 2];
+#pragma unroll
+      for (int i = 0; i < kChunk; i += 2) {
+        const float p0 = ex2(fmaf(x[i], sl2, nbase));
+        const float p1 = ex2(fmaf(x[i + 1], sl2, nbase));
+        ps += p0 + p1;
+        phi[i / 2] = pack2<T>(p0, p1);
+        if (kSplit) plo[i / 2] = pack2<T>(p0 - lo_half<T>(phi[i / 2]), p1 - hi_half<T>(phi[i / 2]));
+      }
+      l = l * alpha + ps;
+
+      // P buffer sb is free once the PV of chunk j-2 completed
+      if (j >= 2 && !mbar_wait_bounded(smem_addr(&pv_done[sb]), (uint32_t)(((j - 2) >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      // O rescale (warp-collective TMEM load/store) after the PV of chunk j-1
+      if (__any_sync(0xffffffffu, move && j > 0)) {
+        if (!mbar_wait_bounded(smem_addr(&pv_done[(j - 1) & 1]), (uint32_t)(((j - 1) >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+        const float a = (move && j > 0) ? alpha : 1.f;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem_o + c0 + lane_base, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
+          tmem_st32(tmem_o + c0 + lane_base, o);
+        }
+        tmem_wait_st();
+      }
+      // P row (K-major, swizzled): 64 tokens x 2 B = 8 chunks of 16 B
+      uint8_t* phi_buf = s_p + (2 * sb) * P_BYTES;
+      uint8_t* plo_buf = s_p + (2 * sb + 1) * P_BYTES;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        *reinterpret_cast<uint4*>(phi_buf + sw128_chunk(r, c)) =
+            make_uint4(phi[4 * c], phi[4 * c + 1], phi[4 * c + 2], phi[4 * c + 3]);
+        if (kSplit)
+          *reinterpret_cast<uint4*>(plo_buf + sw128_chunk(r, c)) =
+              make_uint4(plo[4 * c], plo[4 * c + 1], plo[4 * c + 2], plo[4 * c + 3]);
+      }
+      // tail chunk: V rows at or past L hold stale data; zero them (P is 0 there)
+      const int valid = L - tok0;
+      if (valid < kChunk) {
+        uint8_t* vbase = s_kv + (j % S) * KV_BYTES + HALVES * HALF_BYTES;
+        const int nrows = kChunk - valid;
+        for (int i = tid; i < nrows * HALVES * 8; i += 128) {
+          const int row = valid + i / (HALVES * 8);
+          const int rem = i % (HALVES * 8);
+          *reinterpret_cast<uint4*>(vbase + (rem >> 3) * HALF_BYTES + row * 128 + (rem & 7) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      fence_proxy_async_smem();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&p_full[sb]));
+    }
+
+    // ---- epilogue: O / l -> global ----
+    if (ok && n_chunks > 0) {
+      const int jl = n_chunks - 1;
+      ok = mbar_wait_bounded(smem_addr(&pv_done[jl & 1]), (uint32_t)((jl >> 1) & 1));
+    }
+    if (!ok && lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
+    tmem_fence_after();
+    T* orow = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
+              (long long)t * p.o_st;
+    const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
+#pragma unroll
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t o[32];
+      if (n_chunks > 0) {
+        tmem_ld32(tmem_o + c0 + lane_base, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
+      }
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 v;
+          v.x = pack2<T>(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
+          v.y = pack2<T>(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+          v.z = pack2<T>(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+          v.w = pack2<T>(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c0 + i) = v;
+        }
+      }
+    }
+  }
+
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+size_t prefill_umma_smem_bytes(int D) {
+  const size_t halves = (size_t)D / 64;
+  return 1024 + (size_t)kUmmaStages * 2 * halves * kChunk * 128 + halves * 128 * 128 + 4 * 128 * 128 + 256;
+}
+
+template <typename T, int D>
+static cudaError_t launch_umma_impl(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, bool pdl,
+                                    cudaStream_t stream) {
+  const size_t smem = prefill_umma_smem_bytes(D);
+  static bool prepared[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !prepared[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_umma_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    prepared[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((long long)p.B * p.Hkv * ((p.GQ + 127) / 128)));
+  cfg.blockDim = dim3(kUmmaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, prefill_umma_kernel<T, D>, tmk, tmv, p);
+}
+
+cudaError_t launch_prefill_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
+                                bool pdl, cudaStream_t stream) {
+  if (dtype == PA_DTYPE_BFLOAT16) {
+    if (p.D == 128) return launch_umma_impl<__nv_bfloat16, 128>(p, tmk, tmv, pdl, stream);
+    if (p.D == 64) return launch_umma_impl<__nv_bfloat16, 64>(p, tmk, tmv, pdl, stream);
+  } else if (dtype == PA_DTYPE_FLOAT16) {
+    if (p.D == 128) return launch_umma_impl<__half, 128>(p, tmk, tmv, pdl, stream);
+    if (p.D == 64) return launch_umma_impl<__half, 64>(p, tmk, tmv, pdl, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace pa

@@ -191,6 +191,12 @@ PA_API int pa_read_device_errors(void* device_word, uint32_t* host_flags, int32_
 /* Text for the last failure on this host thread ("" when none). */
 PA_API const char* pa_last_error(void);
 
+/* Name of the kernel the last pa_decode call on this host thread launched
+ * ("pa::decode_mma_kernel", "pa::decode_f32_kernel", "pa::prefill_mma_kernel"
+ * or "pa::prefill_umma_kernel").  No counterpart in the reference, whose
+ * dispatch (paged_attention_triton.py:460-552) is visible in Python. */
+PA_API const char* pa_last_kernel(void);
+
 /* Library version: major * 10000 + minor * 100 + patch. */
 PA_API int32_t pa_version(void);
 

@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "pa_workspace_init",
     "pa_read_device_errors",
     "pa_last_error",
+    "pa_last_kernel",
     "pa_version",
 )
 
@@ -129,6 +130,8 @@ def load() -> ctypes.CDLL:
         lib.pa_read_device_errors.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint32), _i32, _vp]
         lib.pa_last_error.restype = ctypes.c_char_p
         lib.pa_last_error.argtypes = []
+        lib.pa_last_kernel.restype = ctypes.c_char_p
+        lib.pa_last_kernel.argtypes = []
         lib.pa_version.restype = _i32
         lib.pa_version.argtypes = []
         _handle = lib
@@ -138,6 +141,12 @@ def load() -> ctypes.CDLL:
 def last_error() -> str:
     msg = load().pa_last_error()
     return msg.decode() if msg else ""
+
+
+def last_kernel() -> str:
+    """Kernel launched by the last pa_decode call on this host thread."""
+    name = load().pa_last_kernel()
+    return name.decode() if name else ""
 
 
 def check(status: int, what: str) -> None:

@@ -18,6 +18,8 @@
 namespace {
 
 thread_local char g_last_error[512] = "";
+// Kernel launched by the last successful pa_decode on this host thread.
+thread_local const char* g_last_kernel = "";
 
 int fail(int status, const char* fmt, ...) {
   va_list ap;
@@ -164,6 +166,8 @@ size_t ws_partial_bytes(int nw_total, int slot_rows, int D) {
 extern "C" {
 
 const char* pa_last_error(void) { return g_last_error; }
+
+const char* pa_last_kernel(void) { return g_last_kernel; }
 
 int32_t pa_version(void) { return 1 * 10000 + 0 * 100 + 0; }
 
@@ -347,6 +351,7 @@ int pa_decode(const pa_decode_args* a, void* stream) {
       return fail(PA_ERR_UNSUPPORTED, "fp32 decode supports head_dim 32/64/128, got %d", D);
     if (!aligned_ptr(a->key_cache.data, 4) || !aligned_ptr(a->value_cache.data, 4))
       return fail(PA_ERR_UNSUPPORTED, "cache base must be 4-byte aligned");
+    g_last_kernel = "pa::decode_f32_kernel";
     e = pa::launch_decode_f32(p, pdl, strm);
     if (e != cudaSuccess) return cuda_fail(e, "decode_f32 launch");
     return PA_OK;
@@ -401,14 +406,17 @@ int pa_decode(const pa_decode_args* a, void* stream) {
                         ((a->query_stride_b | a->query_stride_h | a->query_stride_t | a->out_stride_b |
                           a->out_stride_h | a->out_stride_t) & 7) == 0;
     if (rows16 && multiquery_policy() != kPolicyMma) {
+      g_last_kernel = "pa::prefill_umma_kernel";
       e = pa::launch_prefill_umma(p, tmk, tmv, dtype, pdl, strm);
       if (e != cudaSuccess) return cuda_fail(e, "tcgen05 multi-query launch");
     } else {
+      g_last_kernel = "pa::prefill_mma_kernel";
       e = pa::launch_prefill_mma(p, tmk, tmv, dtype, pdl, strm);
       if (e != cudaSuccess) return cuda_fail(e, "multi-query launch");
     }
     return PA_OK;
   }
+  g_last_kernel = "pa::decode_mma_kernel";
   e = pa::launch_decode_mma(p, tmk, tmv, dtype, grid, smem, pdl, strm);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return PA_OK;

@@ -211,6 +211,8 @@ def main() -> None:
                     help="override the workload's per-GPU batch (smaller cases for ncu captures)")
     ap.add_argument("--graph", action="store_true",
                     help="time replays of a CUDA graph holding the step (append + decode) instead of eager calls")
+    ap.add_argument("--prefix-sharing", choices=["auto", "on", "off"], default="auto",
+                    help="cascade over shared prompt prefixes (auto: when the workload has them)")
     ap.add_argument("--shard", choices=["auto", "seq", "head"], default="auto",
                     help="multi-GPU layout: sequences (weak scaling) or KV heads + NCCL all-gather "
                          "(strong scaling); auto = heads for cfg5-llama3-70b, sequences otherwise")
@@ -257,6 +259,13 @@ def main() -> None:
         gather = None
     B, q = w.batch, w.q_len
     out = torch.empty_like(w.query)
+    # Shared prompt prefixes (config 4): one group description per batch
+    # composition, passed with every call (paged_attention_decode(prefix_groups=)).
+    pg = None
+    if args.prefix_sharing != "off" and gather is None:
+        pg = w.shared_prefixes()
+    if args.prefix_sharing == "on" and pg is None:
+        raise SystemExit("--prefix-sharing on needs a workload with shared prefixes on the sequence-sharded path")
     graph = None
     if args.graph:
         if gather is not None:
@@ -264,7 +273,7 @@ def main() -> None:
         from llm_serving_runtime_b200.cuda_graph import DecodeStepGraph
 
         graph = DecodeStepGraph([w.key_cache], [w.value_cache], batch=B, max_blocks=w.block_tables.shape[1],
-                                num_q_heads=w.query.shape[1], q_len=q, scale=w.scale)
+                                num_q_heads=w.query.shape[1], q_len=q, scale=w.scale, prefix_groups=pg)
         graph.query[0].copy_(w.query)
         graph.new_key[0].copy_(w.new_key)
         graph.new_value[0].copy_(w.new_value)
@@ -279,7 +288,7 @@ def main() -> None:
             return gather(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
                           w.slot_mapping, w.new_key, w.new_value, out=out)
         return paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens,
-                                      w.scale, w.slot_mapping, w.new_key, w.new_value, out=out)
+                                      w.scale, w.slot_mapping, w.new_key, w.new_value, out=out, prefix_groups=pg)
 
     def barrier():
         if world > 1:
@@ -324,7 +333,7 @@ def main() -> None:
     for i in range(n_dec):
         starts[i].record(stream)
         paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
-                               out=out)
+                               out=out, prefix_groups=pg)
         ends[i].record(stream)
     torch.cuda.synchronize()
     dec_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
@@ -351,8 +360,13 @@ def main() -> None:
     # and step i-1's download overlap step i's decode (how a serving loop hides
     # the PCIe transfers).
     names = ("query", "new_key", "new_value", "slot_mapping", "context_lens", "block_tables")
-    host_in = [{k: getattr(w, k).cpu().pin_memory() for k in names} for _ in range(2)]
-    dev_in = [{k: torch.empty_like(getattr(w, k)) for k in names} for _ in range(2)]
+    pg_names = ("member_offsets", "member_seqs", "prefix_lens", "seq_group") if pg is not None else ()
+
+    def _src(k):
+        return getattr(pg, k) if k in pg_names else getattr(w, k)
+
+    host_in = [{k: _src(k).cpu().pin_memory() for k in names + pg_names} for _ in range(2)]
+    dev_in = [{k: torch.empty_like(_src(k)) for k in names + pg_names} for _ in range(2)]
     dev_out = [torch.empty_like(out) for _ in range(2)]
     full_out_shape = (B, spec.num_q_heads, q, spec.head_dim) if shard == "head" else tuple(out.shape)
     host_out = [torch.empty(full_out_shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
@@ -368,7 +382,7 @@ def main() -> None:
         s_ = i % 2
         with torch.cuda.stream(up_stream):
             up_stream.wait_event(ev_done[s_])  # decode i-2 no longer reads these inputs
-            for k in names:
+            for k in names + pg_names:
                 dev_in[s_][k].copy_(host_in[s_][k], non_blocking=True)
             ev_in[s_].record(up_stream)
 
@@ -379,8 +393,9 @@ def main() -> None:
         d = dev_in[s_]
         args_ = (d["query"], w.key_cache, w.value_cache, d["block_tables"], d["context_lens"], w.scale,
                  d["slot_mapping"], d["new_key"], d["new_value"])
+        pg_ = dataclasses.replace(pg, **{k: d[k] for k in pg_names}) if pg is not None else None
         res = gather(*args_, out=dev_out[s_]) if gather is not None else \
-            paged_attention_decode(*args_, out=dev_out[s_])
+            paged_attention_decode(*args_, out=dev_out[s_], prefix_groups=pg_)
         ev_done[s_].record(stream)
         return res
 
@@ -450,6 +465,7 @@ def main() -> None:
             if world > 1 else "single",
             "l2": "inputs larger than L2 (no flush)",
             "launch": "cuda-graph replay" if args.graph else "eager",
+            "prefix_sharing": (f"cascade over {pg.num_groups} shared-prefix groups" if pg is not None else "off"),
             "bytes_per_call": call_bytes,
         },
         "hbm_gbs_per_call": call_bytes / (ms_per_step / 1e3) / 1e9,

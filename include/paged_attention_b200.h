@@ -149,6 +149,47 @@ PA_API int pa_kv_append(const pa_kv_append_args* args, void* stream);
  * :414-457 (log-sum-exp combine). */
 PA_API int pa_decode(const pa_decode_args* args, void* stream);
 
+/* Sequences whose block tables start with the same physical blocks (a shared
+ * prompt prefix), in groups.  Device arrays except the two host bounds:
+ *   members of group g  = member_seqs[member_offsets[g] .. member_offsets[g+1])
+ *   prefix_lens[g]      = tokens at positions 0 .. prefix_lens[g]-1 that every
+ *                         member of g reads through the SAME physical blocks
+ *                         (the first member's table is the one read);
+ *   seq_group[b]        = group of batch row b, -1 for a row in no group.
+ * A row belongs to at most one group.  max_members and max_prefix_len bound the
+ * device values (they size the grid); a group with more members or a longer
+ * prefix is an argument error the kernels flag (PA_DEVERR_PREFIX). */
+typedef struct pa_prefix_groups {
+  int32_t num_groups;
+  int32_t max_members;            /* host: >= members of any group */
+  int32_t max_prefix_len;         /* host: >= prefix_lens[g] of any group */
+  const int32_t* member_offsets;  /* [num_groups + 1] */
+  const int32_t* member_seqs;     /* [member_offsets[num_groups]] */
+  const int32_t* prefix_lens;     /* [num_groups] */
+  const int32_t* seq_group;       /* [batch] */
+} pa_prefix_groups;
+
+#define PA_DEVERR_PREFIX 0x10u /* a member's table differs from its group's in the prefix,
+                                  or a group exceeds max_members / max_prefix_len */
+
+/* pa_decode over sequences that share prompt prefixes (cascade attention): each
+ * group's query rows attend the shared prefix blocks together, once per group,
+ * on the tcgen05 multi-query kernel; the decode kernel then attends each
+ * sequence's own tokens and merges both parts (log-sum-exp) before writing the
+ * output.  Same result as pa_decode on the same tables, reading each shared
+ * block once per group instead of once per member.  The reference shares
+ * prefixes by copying blocks (GpuKVBlockPool.copy_blocks,
+ * runtime/phase2/paged_kv_kernel.py:233-250; callers worker_server.py:1266-1272)
+ * and then attends every copy; it has no counterpart of this call.
+ * Needs pa_cascade_workspace_bytes() of workspace.  fp32 calls and calls whose
+ * query / out rows are not 16-byte aligned run pa_decode unchanged. */
+PA_API int pa_decode_cascade(const pa_decode_args* args, const pa_prefix_groups* groups, void* stream);
+
+/* Workspace bytes of pa_decode_cascade: pa_decode's plus the prefix partials. */
+PA_API size_t pa_cascade_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                         int32_t q_len, int32_t head_dim, int32_t dtype, int32_t device,
+                                         int32_t num_groups, int32_t max_members, int32_t max_prefix_len);
+
 /* Size of the scratch array behind pa_decode_static_workspace (16 MiB). */
 #define PA_STATIC_WORKSPACE_BYTES (16u << 20)
 
@@ -191,9 +232,10 @@ PA_API int pa_read_device_errors(void* device_word, uint32_t* host_flags, int32_
 /* Text for the last failure on this host thread ("" when none). */
 PA_API const char* pa_last_error(void);
 
-/* Name of the kernel the last pa_decode call on this host thread launched
- * ("pa::decode_mma_kernel", "pa::decode_f32_kernel", "pa::prefill_mma_kernel"
- * or "pa::prefill_umma_kernel").  No counterpart in the reference, whose
+/* Name of the kernel the last pa_decode / pa_decode_cascade call on this host
+ * thread launched ("pa::decode_mma_kernel", "pa::decode_f32_kernel",
+ * "pa::prefill_mma_kernel", "pa::prefill_umma_kernel", or for the cascade
+ * "pa::prefill_umma_kernel<prefix> + pa::decode_mma_kernel").  No counterpart in the reference, whose
  * dispatch (paged_attention_triton.py:460-552) is visible in Python. */
 PA_API const char* pa_last_kernel(void);
 

@@ -5,6 +5,8 @@ Public entry points
                          context_lens, scale, slot_mapping=None, key=None, value=None)
       the north-star call: fused KV append + paged decode attention
   kv_append(...)                      the KV-append kernel alone
+  prefix_sharing.PrefixGroups         shared prompt prefixes -> cascade decode
+                                      (paged_attention_decode(..., prefix_groups=))
   reference_api                       drop-in for runtime/phase2/paged_attention_triton.py
   kv_block_pool.GpuKVBlockPool        drop-in for runtime/phase2/paged_kv_kernel.py
   block_paged_attention               drop-in HF attention hook
@@ -21,5 +23,6 @@ from .paged_attention import (  # noqa: F401
     paged_attention_decode,
     read_device_errors,
 )
+from .prefix_sharing import PrefixGroups, find_shared_prefixes  # noqa: F401
 
 __version__ = "1.0.0"

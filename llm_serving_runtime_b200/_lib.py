@@ -27,6 +27,7 @@ PA_DEVERR_BLOCK_ID_RANGE = 0x1
 PA_DEVERR_TABLE_UNDERRUN = 0x2
 PA_DEVERR_SLOT_RANGE = 0x4
 PA_DEVERR_WAIT_TIMEOUT = 0x8
+PA_DEVERR_PREFIX = 0x10
 
 PA_STATIC_WORKSPACE_BYTES = 16 << 20
 
@@ -34,6 +35,8 @@ EXPORTED_SYMBOLS = (
     "pa_kv_append",
     "pa_decode",
     "pa_decode_static_workspace",
+    "pa_decode_cascade",
+    "pa_cascade_workspace_bytes",
     "pa_decode_workspace_bytes",
     "pa_workspace_init",
     "pa_read_device_errors",
@@ -100,6 +103,18 @@ class DecodeArgs(ctypes.Structure):
     ]
 
 
+class PrefixGroupsArgs(ctypes.Structure):
+    _fields_ = [
+        ("num_groups", _i32),
+        ("max_members", _i32),
+        ("max_prefix_len", _i32),
+        ("member_offsets", _vp),
+        ("member_seqs", _vp),
+        ("prefix_lens", _vp),
+        ("seq_group", _vp),
+    ]
+
+
 _lock = threading.Lock()
 _handle: ctypes.CDLL | None = None
 
@@ -122,6 +137,10 @@ def load() -> ctypes.CDLL:
         lib.pa_decode.argtypes = [ctypes.POINTER(DecodeArgs), _vp]
         lib.pa_decode_static_workspace.restype = ctypes.c_int
         lib.pa_decode_static_workspace.argtypes = [ctypes.POINTER(DecodeArgs), _vp]
+        lib.pa_decode_cascade.restype = ctypes.c_int
+        lib.pa_decode_cascade.argtypes = [ctypes.POINTER(DecodeArgs), ctypes.POINTER(PrefixGroupsArgs), _vp]
+        lib.pa_cascade_workspace_bytes.restype = _sz
+        lib.pa_cascade_workspace_bytes.argtypes = [_i32] * 10
         lib.pa_decode_workspace_bytes.restype = _sz
         lib.pa_decode_workspace_bytes.argtypes = [_i32, _i32, _i32, _i32, _i32, _i32, _i32]
         lib.pa_workspace_init.restype = ctypes.c_int

@@ -10,6 +10,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "pa_common.cuh"
@@ -149,6 +150,36 @@ size_t workspace_bytes_impl(int slot_rows, int D, int nw_total) {
   return pa::kWsHeaderBytes + pa::ws_counter_bytes(nw_total) + pa::ws_partial_bytes(nw_total, slot_rows, D);
 }
 
+// Cascade prefix pass: how many token ranges (splits) each group's prefix is
+// cut into, and their length.  One split while the (group, kv head, 128-row
+// tile) CTAs alone fill the GPU; otherwise enough ranges of >= 256 tokens to
+// reach one CTA per SM, at most 16.
+struct CascadeShape {
+  int splits, split_tokens;
+  size_t ml_bytes, acc_bytes;
+};
+
+CascadeShape cascade_shape(int num_sms, int num_groups, int max_members, int max_prefix, int Hkv, int GQ,
+                           long long rows, int D) {
+  CascadeShape c;
+  const long long tiles = (long long)num_groups * Hkv * (((long long)max_members * GQ + 127) / 128);
+  const int chunk = pa::kUmmaChunkTokens;
+  const int prefix = max_prefix > 0 ? max_prefix : 0;
+  int splits = 1;
+  if (tiles > 0 && tiles < num_sms) {
+    const long long want = (num_sms + tiles - 1) / tiles;
+    const long long by_len = (prefix + 255) / 256;
+    splits = (int)std::max(1LL, std::min({want, by_len, 16LL}));
+  }
+  int per = (prefix + splits - 1) / splits;
+  per = std::max(chunk, (per + chunk - 1) / chunk * chunk);
+  c.split_tokens = per;
+  c.splits = std::max(1, (prefix + per - 1) / per);
+  c.ml_bytes = round_up((size_t)c.splits * rows * 8);
+  c.acc_bytes = round_up((size_t)c.splits * rows * D * 4);
+  return c;
+}
+
 }  // namespace
 
 namespace pa {
@@ -266,7 +297,39 @@ int pa_kv_append(const pa_kv_append_args* a, void* stream) {
   return PA_OK;
 }
 
-int pa_decode(const pa_decode_args* a, void* stream) {
+size_t pa_cascade_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t q_len,
+                                  int32_t head_dim, int32_t dtype, int32_t device, int32_t num_groups,
+                                  int32_t max_members, int32_t max_prefix_len) {
+  const size_t base = pa_decode_workspace_bytes(batch, num_q_heads, num_kv_heads, q_len, head_dim, dtype, device);
+  if (base == 0 || dtype == PA_DTYPE_FLOAT32 || num_groups <= 0) return base;
+  if (max_members <= 0 || max_prefix_len < 0) return 0;
+  DeviceInfo* info = nullptr;
+  if (device_info(device, &info) != PA_OK) return 0;
+  const DecodeShape s = decode_shape(num_q_heads, num_kv_heads, q_len);
+  const CascadeShape c = cascade_shape(info->num_sms, num_groups, max_members, max_prefix_len, num_kv_heads, s.GQ,
+                                       (long long)batch * num_q_heads * q_len, head_dim);
+  return base + c.ml_bytes + c.acc_bytes;
+}
+
+static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, void* stream);
+
+int pa_decode(const pa_decode_args* a, void* stream) { return decode_impl(a, nullptr, stream); }
+
+int pa_decode_cascade(const pa_decode_args* a, const pa_prefix_groups* grp, void* stream) {
+  g_last_error[0] = 0;
+  if (grp == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null prefix groups");
+  if (grp->num_groups < 0) return fail(PA_ERR_INVALID_ARGUMENT, "num_groups must not be negative");
+  if (grp->num_groups > 0) {
+    if (grp->member_offsets == nullptr || grp->member_seqs == nullptr || grp->prefix_lens == nullptr ||
+        grp->seq_group == nullptr)
+      return fail(PA_ERR_INVALID_ARGUMENT, "prefix groups need member_offsets, member_seqs, prefix_lens, seq_group");
+    if (grp->max_members <= 0 || grp->max_prefix_len < 0)
+      return fail(PA_ERR_INVALID_ARGUMENT, "max_members must be positive and max_prefix_len non-negative");
+  }
+  return decode_impl(a, grp->num_groups > 0 ? grp : nullptr, stream);
+}
+
+static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, void* stream) {
   g_last_error[0] = 0;
   if (a == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null args");
   const int dtype = a->dtype;
@@ -364,21 +427,51 @@ int pa_decode(const pa_decode_args* a, void* stream) {
     return fail(PA_ERR_UNSUPPORTED, "fp16/bf16 decode needs a power-of-two block_size in [8, 256], got %d", bs);
   const int grid = info->num_sms;
   p.nw_total = grid * pa::kDecodeWarps;
-  const size_t need = workspace_bytes_impl(p.slot_rows, D, p.nw_total);
+  // tcgen05 kernels: each thread moves its query (and output) row in 16-byte pieces.
+  const bool q_rows16 = aligned_ptr(a->query, 16) &&
+                        ((a->query_stride_b | a->query_stride_h | a->query_stride_t) & 7) == 0;
+  const bool rows16 = q_rows16 && aligned_ptr(a->out, 16) &&
+                      ((a->out_stride_b | a->out_stride_h | a->out_stride_t) & 7) == 0;
+  // Shared prefixes go through the tcgen05 prefix pass, which needs 16-byte
+  // query rows; without them the plain decode computes the same result.
+  const bool cascade = grp != nullptr && q_rows16;
+  size_t need = workspace_bytes_impl(p.slot_rows, D, p.nw_total);
+  CascadeShape cs = {1, pa::kUmmaChunkTokens, 0, 0};
+  if (cascade) {
+    if ((long long)grp->max_members * s.GQ > (1LL << 30))
+      return fail(PA_ERR_UNSUPPORTED, "max_members * rows per kv head too large");
+    cs = cascade_shape(info->num_sms, grp->num_groups, grp->max_members, grp->max_prefix_len, p.Hkv, p.GQ,
+                       (long long)p.B * p.Hq * p.q_len, D);
+  }
+  const size_t decode_need = need;
+  need += cs.ml_bytes + cs.acc_bytes;
   if (a->workspace_bytes < need)
     return fail(PA_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", a->workspace_bytes, need);
   char* ws = static_cast<char*>(a->workspace);
   p.counters = reinterpret_cast<int32_t*>(ws + pa::kWsHeaderBytes);
   p.partials = reinterpret_cast<float*>(ws + pa::kWsHeaderBytes + pa::ws_counter_bytes(p.nw_total));
+  if (cascade) {
+    p.seq_group = grp->seq_group;
+    p.group_prefix = grp->prefix_lens;
+    p.member_off = grp->member_offsets;
+    p.member_seq = grp->member_seqs;
+    p.pre_ml = reinterpret_cast<float2*>(ws + decode_need);
+    p.pre_acc = reinterpret_cast<float*>(ws + decode_need + cs.ml_bytes);
+    p.num_groups = grp->num_groups;
+    p.max_members = grp->max_members;
+    p.max_prefix = grp->max_prefix_len;
+    p.splits = cs.splits;
+    p.split_tokens = cs.split_tokens;
+  }
 
   // Ring depth: as many 16-token stages per warp as shared memory allows (2..8).
   const size_t budget = (size_t)info->max_smem_optin - 64;  // static shared memory of the kernel
   int stages = 8;
-  while (stages >= 2 && pa::decode_mma_smem_bytes(D, p.B, stages) > budget) --stages;
+  while (stages >= 2 && pa::decode_mma_smem_bytes(D, p.B, stages, cascade) > budget) --stages;
   if (stages < 2)
     return fail(PA_ERR_UNSUPPORTED, "batch %d too large for the decode kernel's shared memory", p.B);
   p.stages = stages;
-  const size_t smem = pa::decode_mma_smem_bytes(D, p.B, stages);
+  const size_t smem = pa::decode_mma_smem_bytes(D, p.B, stages, cascade);
 
   CUtensorMap tmk, tmv;
   st = encode_cache_map(&tmk, a->key_cache, dtype, D, bs, p.Hkv, "key_cache");
@@ -400,11 +493,17 @@ int pa_decode(const pa_decode_args* a, void* stream) {
   // 128-row tiles to fill the GPU: the multi-query kernel shares each K/V tile
   // across 128 rows.  Otherwise the split-K decode kernel.
   const long long prefill_tiles = (long long)p.B * p.Hkv * ((p.GQ + 127) / 128);
+  if (cascade) {
+    // Prefix pass (tcgen05), then the decode kernel over each member's own
+    // tokens, which folds the prefix states in; it waits for the prefix grid.
+    g_last_kernel = "pa::prefill_umma_kernel<prefix> + pa::decode_mma_kernel";
+    e = pa::launch_prefix_umma(p, tmk, tmv, dtype, pdl, strm);
+    if (e != cudaSuccess) return cuda_fail(e, "cascade prefix launch");
+    e = pa::launch_decode_mma(p, tmk, tmv, dtype, grid, smem, true, strm);
+    if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+    return PA_OK;
+  }
   if (p.GQ >= 64 && prefill_tiles >= info->num_sms) {
-    // tcgen05 kernel: each thread moves its query / output row in 16-byte pieces.
-    const bool rows16 = aligned_ptr(a->query, 16) && aligned_ptr(a->out, 16) &&
-                        ((a->query_stride_b | a->query_stride_h | a->query_stride_t | a->out_stride_b |
-                          a->out_stride_h | a->out_stride_t) & 7) == 0;
     if (rows16 && multiquery_policy() != kPolicyMma) {
       g_last_kernel = "pa::prefill_umma_kernel";
       e = pa::launch_prefill_umma(p, tmk, tmv, dtype, pdl, strm);

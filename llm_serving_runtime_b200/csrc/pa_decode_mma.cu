@@ -76,6 +76,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kDecodeWarps * stages * STAGE_BYTES);
   int* s_lens = reinterpret_cast<int*>(bars + kDecodeWarps * stages);
   int* s_pref = s_lens + p.B;
+  // Cascade (shared prefixes): the prefix kernel has attended each member's
+  // first s_u0[b] units; the work list starts every sequence after them.
+  int* s_u0 = s_pref + p.B + 1;
+  const bool cascade = p.seq_group != nullptr;
   __shared__ int s_warp_tot[kDecodeWarps];
 
   const int tid = threadIdx.x;
@@ -109,8 +113,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       }
       if (L < 0) L = 0;
       s_lens[b] = L;
+      int u0 = 0;
+      if (cascade) {
+        const int gi = p.seq_group[b];
+        if (gi >= 0 && gi < p.num_groups) u0 = cascade_prefix_tokens(p, gi) / kUnitTokens;
+        s_u0[b] = u0;
+      }
       int units = 0;
-      for (int mg = 0; mg < p.NMG; ++mg) units += group_units(L, mg, p);
+      for (int mg = 0; mg < p.NMG; ++mg) units += max(0, group_units(L, mg, p) - u0);
       local += units * p.Hkv;
     }
     int incl = local;
@@ -126,7 +136,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     for (int b = beg; b < end; ++b) {
       s_pref[b] = run;
       int units = 0;
-      for (int mg = 0; mg < p.NMG; ++mg) units += group_units(s_lens[b], mg, p);
+      for (int mg = 0; mg < p.NMG; ++mg) units += max(0, group_units(s_lens[b], mg, p) - (cascade ? s_u0[b] : 0));
       run += units * p.Hkv;
     }
     if (tid == nthr - 1) s_pref[B] = run;
@@ -134,26 +144,57 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   fence_mbar_init();
   __syncthreads();
 
-  // Row groups with nothing to attend get no unit: their rows are zero.
-  for (int b = blockIdx.x; b < B; b += gridDim.x) {
-    for (int mg = 0; mg < p.NMG; ++mg) {
-      if (group_units(s_lens[b], mg, p) != 0) continue;
-      const int rows = min(16, p.GQ - 16 * mg);
-      for (int i = tid; i < p.Hkv * rows * (D / 2); i += blockDim.x) {
-        const int d2 = i % (D / 2);
-        const int hr = i / (D / 2);
-        const int h = hr / rows;
-        const int qr = 16 * mg + (hr - h * rows);
-        const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
-        T* o = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
-               (long long)t * p.o_st + 2 * d2;
-        *reinterpret_cast<uint32_t*>(o) = 0u;
+  // Units of row group mg of sequence b in the work list.
+  auto units_of = [&](int b, int mg) -> int {
+    const int n = group_units(s_lens[b], mg, p);
+    return cascade ? max(0, n - s_u0[b]) : n;
+  };
+
+  // Row groups with nothing to attend get no unit: their rows are zero, or,
+  // under the cascade, the normalised prefix part alone.
+  auto fill_empty_rows = [&]() {
+    const long long R = (long long)B * p.Hq * p.q_len;
+    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+      const bool pre = cascade && s_u0[b] > 0;
+      for (int mg = 0; mg < p.NMG; ++mg) {
+        if (units_of(b, mg) != 0) continue;
+        const int rows = min(16, p.GQ - 16 * mg);
+        for (int i = tid; i < p.Hkv * rows * (D / 2); i += blockDim.x) {
+          const int d2 = i % (D / 2);
+          const int hr = i / (D / 2);
+          const int h = hr / rows;
+          const int qr = 16 * mg + (hr - h * rows);
+          const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
+          T* o = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
+                 (long long)t * p.o_st + 2 * d2;
+          uint32_t v = 0u;
+          if (pre) {
+            const long long ridx = ((long long)b * p.Hq + h * p.G + g) * p.q_len + t;
+            const float M = prefix_max(p, ridx, R);
+            const float base = (M == -INFINITY) ? 0.f : M;
+            float lsum = 0.f, a0 = 0.f, a1 = 0.f;
+            for (int s = 0; s < p.splits; ++s) {
+              const float2 ml = __ldcg(&p.pre_ml[s * R + ridx]);
+              const float w = ex2(ml.x - base);
+              const float2 a = __ldcg(reinterpret_cast<const float2*>(p.pre_acc + (s * R + ridx) * D + 2 * d2));
+              lsum += w * ml.y;
+              a0 = fmaf(w, a.x, a0);
+              a1 = fmaf(w, a.y, a1);
+            }
+            const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+            v = pack2<T>(a0 * inv, a1 * inv);
+          }
+          *reinterpret_cast<uint32_t*>(o) = v;
+        }
       }
     }
-  }
+  };
+  if (!cascade) fill_empty_rows();
 
-  // Everything below reads the KV cache, which the previous kernel may write.
+  // Everything below reads the KV cache, which the previous kernel may write
+  // (and, under the cascade, the prefix states the previous kernel leaves).
   pdl_wait_previous();
+  if (cascade) fill_empty_rows();
 
   const long long W = s_pref[B];
   if (W == 0) return;
@@ -184,10 +225,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     int off = (int)(ws - s_pref[lo]);
     start.h = off / S;
     off -= start.h * S;
-    const int L = s_lens[lo];
     start.mg = 0;
     while (true) {
-      const int n = group_units(L, start.mg, p);
+      const int n = units_of(lo, start.mg);
       if (off < n) {
         start.n = n;
         break;
@@ -208,7 +248,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           if (++c.b >= B) return;
         }
       }
-      c.n = group_units(s_lens[c.b], c.mg, p);
+      c.n = units_of(c.b, c.mg);
     } while (c.n == 0);
   };
 
@@ -236,7 +276,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     const int h = pc.h;
     const uint32_t stage = my_ring + (uint32_t)slot * STAGE_BYTES;
     const uint32_t bar = my_bars + (uint32_t)slot * 8u;
-    const int tok0 = pc.u * kUnitTokens;
+    const int tok0 = (pc.u + (cascade ? s_u0[pc.b] : 0)) * kUnitTokens;
     if (bs >= kUnitTokens) {
       const int lb = tok0 / bs;
       const int y = tok0 - lb * bs;
@@ -358,8 +398,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     const uint32_t vbase = kbase + TILE_BYTES;
 
     // ---- QK^T, masked online softmax, PV on tensor cores ----
-    attend_unit<T, D>(kbase, vbase, qa, o_acc, m0, m1, l0, l1, cc.u * kUnitTokens, L, lim0, lim1, mask_from,
-                      p.scale_log2, lane);
+    attend_unit<T, D>(kbase, vbase, qa, o_acc, m0, m1, l0, l1, (cc.u + (cascade ? s_u0[b] : 0)) * kUnitTokens, L,
+                      lim0, lim1, mask_from, p.scale_log2, lane);
 
     // ---- refill this slot with the unit `stages` ahead ----
     __syncwarp();
@@ -396,7 +436,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           op1 = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
                 (long long)t * p.o_st;
         }
-        store_rows<T, D>(op0, op1, o_acc, lt0, lt1, quad);
+        if (cascade && s_u0[b] > 0) {
+          const long long rb = (long long)b * p.Hq + h * p.G;
+          const int qa0 = mg * 16 + qrow0, qa1 = qa0 + 8;
+          const long long ridx0 = (rb + qa0 % p.G) * p.q_len + qa0 / p.G;
+          const long long ridx1 = (rb + qa1 % p.G) * p.q_len + qa1 / p.G;
+          store_rows_folded<T, D>(op0, op1, o_acc, m0, m1, lt0, lt1, ridx0, ridx1, p, quad);
+        } else {
+          store_rows<T, D>(op0, op1, o_acc, lt0, lt1, quad);
+        }
       } else {
         // Partial: (m, l, acc) to this warp's slot, then count the arrival.
         const int slot_idx = 2 * gw + (piece_first ? 0 : 1);
@@ -506,9 +554,27 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
 #pragma unroll
               for (int o = 16; o > 0; o >>= 1) lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], o);
               if (rg + r < rows_here) {
-                const float inv = lsum[r] > 0.f ? 1.f / lsum[r] : 0.f;
                 const int qr = mg * 16 + rg + r;
                 const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
+                if (cascade && s_u0[b] > 0) {
+                  // fold the row's prefix part (one (m, l, acc) per split)
+                  const long long R = (long long)B * p.Hq * p.q_len;
+                  const long long ridx = ((long long)b * p.Hq + h * p.G + g) * p.q_len + t;
+                  const float M2 = fmaxf(M[r], prefix_max(p, ridx, R));
+                  const float c = ex2(M[r] - M2);
+                  lsum[r] *= c;
+#pragma unroll
+                  for (int k = 0; k < DPL; ++k) acc[r][k] *= c;
+                  for (int s = 0; s < p.splits; ++s) {
+                    const float2 ml = __ldcg(&p.pre_ml[s * R + ridx]);
+                    const float w = ex2(ml.x - M2);
+                    lsum[r] += w * ml.y;
+                    const float* a = p.pre_acc + (s * R + ridx) * D;
+#pragma unroll
+                    for (int k = 0; k < DPL; ++k) acc[r][k] = fmaf(w, __ldcg(a + lane + 32 * k), acc[r][k]);
+                  }
+                }
+                const float inv = lsum[r] > 0.f ? 1.f / lsum[r] : 0.f;
                 T* op = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
                         (long long)t * p.o_st;
 #pragma unroll
@@ -527,10 +593,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   }
 }
 
-size_t decode_mma_smem_bytes(int D, int B, int stages) {
+size_t decode_mma_smem_bytes(int D, int B, int stages, bool cascade) {
   const size_t stage_bytes = 2u * 16u * (size_t)D * 2u;
   return 1024 + (size_t)kDecodeWarps * stages * stage_bytes + (size_t)kDecodeWarps * stages * 8 +
-         (size_t)(2 * B + 1) * 4;
+         (size_t)((cascade ? 3 : 2) * B + 1) * 4;
 }
 
 template <typename T, int D>

@@ -51,6 +51,20 @@ struct DecodeParams {
   int32_t slot_rows; // rows stored per partial slot
   int32_t nw_total;  // warps in the grid
   int32_t stages;    // shared-memory ring depth per warp
+  // Shared prompt prefixes (pa_decode_cascade); seq_group is null otherwise.
+  // The prefix kernel attends group g's member rows over tokens [0, P_g) with
+  // P_g = prefix_lens[g] rounded down to whole 16-token units, in `splits`
+  // ranges of split_tokens, and leaves per split and query row (b, hq, t)
+  // (m, l) in pre_ml and the unnormalised accumulator in pre_acc, at row index
+  // (b * Hq + hq) * q_len + t.  The decode kernel starts each member at P_g
+  // and folds those states into its rows.
+  const int32_t* seq_group;     // [B] group of each row, -1: none
+  const int32_t* group_prefix;  // [num_groups] shared tokens
+  const int32_t* member_off;    // [num_groups + 1]
+  const int32_t* member_seq;    // member rows
+  float2* pre_ml;               // [splits][B * Hq * q_len]
+  float* pre_acc;               // [splits][B * Hq * q_len][D]
+  int32_t num_groups, max_members, max_prefix, splits, split_tokens;
 };
 
 struct AppendParams {
@@ -90,9 +104,15 @@ cudaError_t launch_prefill_mma(const DecodeParams& p, const CUtensorMap& tmk, co
                                bool pdl, cudaStream_t stream);
 cudaError_t launch_prefill_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
                                 bool pdl, cudaStream_t stream);
+// Prefix part of pa_decode_cascade (tcgen05): one CTA per (split, group, kv head,
+// 128-row tile of the group's member rows).
+cudaError_t launch_prefix_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
+                               bool pdl, cudaStream_t stream);
+// Tokens per chunk of the tcgen05 kernels (prefix split ranges are multiples of it).
+constexpr int kUmmaChunkTokens = 64;
 
 // Shared-memory bytes of the tensor-core kernel for given stage count.
-size_t decode_mma_smem_bytes(int D, int B, int stages);
+size_t decode_mma_smem_bytes(int D, int B, int stages, bool cascade);
 // Opt a kernel instantiation into large dynamic shared memory (once per device).
 cudaError_t decode_mma_prepare(int dtype, int D, size_t smem);
 

@@ -112,7 +112,13 @@ __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) { return (uint32_t
 
 }  // namespace
 
-template <typename T, int D>
+// kPrefix = false: a CTA owns a 128-row tile of one (sequence, kv head) and
+// writes normalised output rows.  kPrefix = true (the prefix part of
+// pa_decode_cascade): a CTA owns a 128-row tile of the member rows of one
+// (split, prefix group, kv head) -- row r is row r % GQ of member r / GQ --
+// attends the group's shared blocks in the split's token range through the
+// first member's block table, and leaves (m, l, unnormalised O) per row.
+template <typename T, int D, bool kPrefix>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
     prefill_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                         const DecodeParams p) {
@@ -143,24 +149,61 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int BH = p.B * p.Hkv;
-  const int MT = (p.GQ + 127) / 128;
-  const int mt = MT - 1 - (int)(blockIdx.x / BH);  // latest (heaviest) tiles first
-  const int bh = (int)(blockIdx.x % BH);
-  const int b = bh / p.Hkv;
-  const int h = bh - b * p.Hkv;
-
-  int L = p.context_lens[b] + p.len_offset;
   const int cap = p.max_blocks * p.bs;
-  if (L > cap) {
-    if (tid == 0 && h == 0 && mt == MT - 1) raise_flag(p.status, PA_DEVERR_TABLE_UNDERRUN);
-    L = cap;
+  // Tile: the sequence whose block table is read (b_kv), the kv head, the first
+  // row, the rows that exist, and the token range [kv_lo, kv_end) streamed in
+  // n_chunks chunks (tokens at or past kv_end are never attended).
+  int b_kv, h, row0, rows_total, kv_lo, kv_end, n_chunks;
+  int moff = 0, split = 0, prefix_tokens = 0;
+  if constexpr (kPrefix) {
+    const int MT = (p.max_members * p.GQ + 127) / 128;
+    int idx = (int)blockIdx.x;
+    const int mt = idx % MT;
+    idx /= MT;
+    h = idx % p.Hkv;
+    idx /= p.Hkv;
+    const int gi = idx % p.num_groups;
+    split = idx / p.num_groups;
+    moff = p.member_off[gi];
+    int nmem = p.member_off[gi + 1] - moff;
+    if (nmem > p.max_members || p.group_prefix[gi] > p.max_prefix) {
+      if (tid == 0 && h == 0 && mt == 0 && split == 0) raise_flag(p.status, PA_DEVERR_PREFIX);
+      nmem = min(nmem, p.max_members);
+    }
+    if (nmem < 0) nmem = 0;
+    prefix_tokens = cascade_prefix_tokens(p, gi);
+    rows_total = nmem * p.GQ;
+    row0 = mt * 128;
+    kv_lo = split * p.split_tokens;
+    kv_end = min(prefix_tokens, kv_lo + p.split_tokens);
+    b_kv = nmem > 0 ? p.member_seq[moff] : 0;
+    if (b_kv < 0 || b_kv >= p.B) {  // the group's table row must be a batch row
+      if (tid == 0) raise_flag(p.status, PA_DEVERR_PREFIX);
+      b_kv = 0;
+      rows_total = 0;
+    }
+    n_chunks = (row0 < rows_total && kv_end > kv_lo) ? (kv_end - kv_lo + kChunk - 1) / kChunk : 0;
+  } else {
+    const int BH = p.B * p.Hkv;
+    const int MT = (p.GQ + 127) / 128;
+    const int mt = MT - 1 - (int)(blockIdx.x / BH);  // latest (heaviest) tiles first
+    const int bh = (int)(blockIdx.x % BH);
+    b_kv = bh / p.Hkv;
+    h = bh - b_kv * p.Hkv;
+    int L = p.context_lens[b_kv] + p.len_offset;
+    if (L > cap) {
+      if (tid == 0 && h == 0 && mt == MT - 1) raise_flag(p.status, PA_DEVERR_TABLE_UNDERRUN);
+      L = cap;
+    }
+    if (L < 0) L = 0;
+    row0 = mt * 128;
+    rows_total = p.GQ;
+    const int rows_tile = min(128, p.GQ - row0);
+    const int lim_tile = L - p.q_len + (row0 + rows_tile - 1) / p.G;
+    kv_lo = 0;
+    kv_end = L;
+    n_chunks = lim_tile < 0 ? 0 : (lim_tile + kChunk) / kChunk;
   }
-  if (L < 0) L = 0;
-  const int row0 = mt * 128;
-  const int rows_tile = min(128, p.GQ - row0);
-  const int lim_tile = L - p.q_len + (row0 + rows_tile - 1) / p.G;
-  const int n_chunks = lim_tile < 0 ? 0 : (lim_tile + kChunk) / kChunk;
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -191,6 +234,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   const uint32_t tmem_s0 = tmem;        // columns 0..63 / 64..127: S buffers
   const uint32_t tmem_o = tmem + 128;   // columns 128 .. 128 + D - 1: O
   pdl_wait_previous();
+  // The cascade's decode kernel may start its prologue now; it waits for this
+  // grid to finish before reading the prefix states.
+  if constexpr (kPrefix) pdl_launch_dependents();
 
   if (warp == 4) {
     // ---------------- producer: K/V chunks by TMA ----------------
@@ -211,35 +257,36 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
       const uint32_t base = smem_addr(s_kv + stage * KV_BYTES);
       const uint32_t bar = smem_addr(&kv_full[stage]);
-      // units of this chunk the sequence reaches
-      const int units = min(4, (L - j * kChunk + 15) / 16);
+      const int chunk0 = kv_lo + j * kChunk;
+      // units of this chunk the token range reaches
+      const int units = min(4, (kv_end - chunk0 + 15) / 16);
       uint32_t tx = 0;
       int physs[4][2];
       for (int u = 0; u < 4; ++u) {
-        const int tok0 = j * kChunk + u * 16;
+        const int tok0 = chunk0 + u * 16;
         const int lb0 = tok0 / bs;
         const int need = bs >= 16 ? 1 : 16 / bs;
         if (win_base < 0 || lb0 < win_base || lb0 + need > win_base + 32) {
           win_base = lb0;
           const int e = lb0 + lane;
-          win_val = (e < p.max_blocks) ? __ldg(&p.block_tables[(long long)b * p.bt_stride + e]) : -1;
+          win_val = (e < p.max_blocks) ? __ldg(&p.block_tables[(long long)b_kv * p.bt_stride + e]) : -1;
         }
         physs[u][0] = __shfl_sync(0xffffffffu, win_val, lb0 - win_base);
         physs[u][1] = __shfl_sync(0xffffffffu, win_val, (lb0 + 1 - win_base) & 31);
       }
       if (lane == 0) {
         for (int u = 0; u < units; ++u) {
-          const int tok0 = j * kChunk + u * 16;
+          const int tok0 = chunk0 + u * 16;
           if (bs >= 16) {
             tx += 2u * HALVES * 2048u;
           } else {
-            const bool need1 = (tok0 / bs + 1) * bs < L;
+            const bool need1 = (tok0 / bs + 1) * bs < kv_end;
             tx += (need1 ? 2u : 1u) * 2u * HALVES * (uint32_t)bs * 128u;
           }
         }
         mbar_arrive_expect_tx(bar, tx);
         for (int u = 0; u < units; ++u) {
-          const int tok0 = j * kChunk + u * 16;
+          const int tok0 = chunk0 + u * 16;
           const int lb0 = tok0 / bs;
           if (bs >= 16) {
             const int phys = physs[u][0];
@@ -251,7 +298,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
               tma_load_4d(base + (HALVES + hf) * HALF_BYTES + u * 2048u, &tmv, bar, hf * 64, y, h, phys);
             }
           } else {
-            const bool need1 = (lb0 + 1) * bs < L;
+            const bool need1 = (lb0 + 1) * bs < kv_end;
             const uint32_t box = (uint32_t)bs * 128u;
             for (int jj = 0; jj < (need1 ? 2 : 1); ++jj) {
               const int phys = physs[u][jj];
@@ -320,19 +367,51 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         issue_pv(j);
       }
       if (!ok) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
+    } else if constexpr (kPrefix) {
+      // Idle lanes: every member must reach the shared prefix through the same
+      // physical blocks as the first member (whose table the producer reads).
+      // Checked once per member, by the split-0 / head-0 tile holding its first row.
+      if (lane > 0 && split == 0 && h == 0 && prefix_tokens > 0) {
+        const int i_lo = (row0 + p.GQ - 1) / p.GQ;
+        const int i_hi = min(rows_total, row0 + 128);  // rows; members i with i*GQ < i_hi
+        const int nblk = (prefix_tokens + p.bs - 1) / p.bs;
+        bool bad = false;
+        for (int i = i_lo; i * p.GQ < i_hi; ++i) {
+          const int bm = p.member_seq[moff + i];
+          if (bm == b_kv) continue;
+          if (bm < 0 || bm >= p.B) {
+            bad = true;
+            continue;
+          }
+          for (int k = lane - 1; k < nblk; k += 31)
+            bad |= __ldg(&p.block_tables[(long long)bm * p.bt_stride + k]) !=
+                   __ldg(&p.block_tables[(long long)b_kv * p.bt_stride + k]);
+        }
+        if (bad) raise_flag(p.status, PA_DEVERR_PREFIX);
+      }
     }
     __syncwarp();
   } else {
     // ---------------- softmax warps: thread = query row = TMEM lane ----------------
     const int r = tid;  // 0..127
     const int qr = row0 + r;
-    const bool row_ok = qr < p.GQ;
-    int t = 0, g = 0;
+    const bool row_ok = qr < rows_total;
+    int t = 0, g = 0, b = b_kv;
+    int lim = -1;  // last attendable position of this row
     if (row_ok) {
-      t = qr / p.G;
-      g = qr - t * p.G;
+      int r_in = qr;
+      if constexpr (kPrefix) {
+        const int i = qr / p.GQ;
+        r_in = qr - i * p.GQ;
+        b = p.member_seq[moff + i];
+        if (b < 0 || b >= p.B) b = b_kv;  // flagged by the table check
+      }
+      t = r_in / p.G;
+      g = r_in - t * p.G;
+      const int Lb = min(max(p.context_lens[b] + p.len_offset, 0), cap);
+      lim = Lb - p.q_len + t;
+      if constexpr (kPrefix) lim = min(lim, kv_end - 1);
     }
-    const int lim = row_ok ? L - p.q_len + t : -1;  // last attendable position
     // Q row -> swizzled K-major tile (row r)
     {
       const T* qrow = static_cast<const T*>(p.q) + (long long)b * p.q_sb + (long long)(h * p.G + g) * p.q_sh +
@@ -375,8 +454,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&s_free[sb]));
 
-      const int tok0 = j * kChunk;
-      if (tok0 + kChunk - 1 > lim) {  // causal / end-of-sequence mask in this chunk
+      const int tok0 = kv_lo + j * kChunk;
+      if (tok0 + kChunk - 1 > lim) {  // causal / end-of-range mask in this chunk
 #pragma unroll
         for (int i = 0; i < kChunk; ++i)
           if (tok0 + i > lim) x[i] = -INFINITY;
@@ -442,8 +521,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           *reinterpret_cast<uint4*>(plo_buf + sw128_chunk(r, c)) =
               make_uint4(plo[4 * c], plo[4 * c + 1], plo[4 * c + 2], plo[4 * c + 3]);
       }
-      // tail chunk: V rows at or past L hold stale data; zero them (P is 0 there)
-      const int valid = L - tok0;
+      // tail chunk: V rows at or past kv_end hold stale data; zero them (P is 0 there)
+      const int valid = kv_end - tok0;
       if (valid < kChunk) {
         uint8_t* vbase = s_kv + (j % S) * KV_BYTES + HALVES * HALF_BYTES;
         const int nrows = kChunk - valid;
@@ -467,6 +546,33 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     }
     if (!ok && lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
     tmem_fence_after();
+    if constexpr (kPrefix) {
+      // (m, l) and the unnormalised O of this row's prefix part, for the decode
+      // kernel to fold in; an empty or failed part is (-inf, 0, 0).
+      const bool have = ok && l > 0.f;
+      const long long ridx = (long long)split * p.B * p.Hq * p.q_len +
+                             ((long long)b * p.Hq + h * p.G + g) * p.q_len + t;
+      if (row_ok) p.pre_ml[ridx] = make_float2(have ? m_ref : -INFINITY, have ? l : 0.f);
+      float* arow = p.pre_acc + ridx * D;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        if (n_chunks > 0) {
+          tmem_ld32(tmem_o + c0 + lane_base, o);
+          tmem_wait_ld();
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (have)
+              v = make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]),
+                              __uint_as_float(o[i + 3]));
+            *reinterpret_cast<float4*>(arow + c0 + i) = v;
+          }
+        }
+      }
+    } else {
     T* orow = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
               (long long)t * p.o_st;
     const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
@@ -492,6 +598,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         }
       }
     }
+    }
   }
 
   tmem_fence_before();
@@ -507,7 +614,7 @@ size_t prefill_umma_smem_bytes(int D) {
   return 1024 + (size_t)kUmmaStages * 2 * halves * kChunk * 128 + halves * 128 * 128 + 4 * 128 * 128 + 256;
 }
 
-template <typename T, int D>
+template <typename T, int D, bool kPrefix>
 static cudaError_t launch_umma_impl(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, bool pdl,
                                     cudaStream_t stream) {
   const size_t smem = prefill_umma_smem_bytes(D);
@@ -515,13 +622,16 @@ static cudaError_t launch_umma_impl(const DecodeParams& p, const CUtensorMap& tm
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !prepared[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_umma_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(prefill_umma_kernel<T, D, kPrefix>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     prepared[dev] = true;
   }
+  const long long tiles =
+      kPrefix ? (long long)p.splits * p.num_groups * p.Hkv * ((p.max_members * p.GQ + 127) / 128)
+              : (long long)p.B * p.Hkv * ((p.GQ + 127) / 128);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((long long)p.B * p.Hkv * ((p.GQ + 127) / 128)));
+  cfg.gridDim = dim3((unsigned)tiles);
   cfg.blockDim = dim3(kUmmaThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -530,19 +640,30 @@ static cudaError_t launch_umma_impl(const DecodeParams& p, const CUtensorMap& tm
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = pdl ? attr : nullptr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, prefill_umma_kernel<T, D>, tmk, tmv, p);
+  return cudaLaunchKernelEx(&cfg, prefill_umma_kernel<T, D, kPrefix>, tmk, tmv, p);
+}
+
+template <bool kPrefix>
+static cudaError_t launch_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
+                               bool pdl, cudaStream_t stream) {
+  if (dtype == PA_DTYPE_BFLOAT16) {
+    if (p.D == 128) return launch_umma_impl<__nv_bfloat16, 128, kPrefix>(p, tmk, tmv, pdl, stream);
+    if (p.D == 64) return launch_umma_impl<__nv_bfloat16, 64, kPrefix>(p, tmk, tmv, pdl, stream);
+  } else if (dtype == PA_DTYPE_FLOAT16) {
+    if (p.D == 128) return launch_umma_impl<__half, 128, kPrefix>(p, tmk, tmv, pdl, stream);
+    if (p.D == 64) return launch_umma_impl<__half, 64, kPrefix>(p, tmk, tmv, pdl, stream);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_prefill_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
                                 bool pdl, cudaStream_t stream) {
-  if (dtype == PA_DTYPE_BFLOAT16) {
-    if (p.D == 128) return launch_umma_impl<__nv_bfloat16, 128>(p, tmk, tmv, pdl, stream);
-    if (p.D == 64) return launch_umma_impl<__nv_bfloat16, 64>(p, tmk, tmv, pdl, stream);
-  } else if (dtype == PA_DTYPE_FLOAT16) {
-    if (p.D == 128) return launch_umma_impl<__half, 128>(p, tmk, tmv, pdl, stream);
-    if (p.D == 64) return launch_umma_impl<__half, 64>(p, tmk, tmv, pdl, stream);
-  }
-  return cudaErrorInvalidValue;
+  return launch_umma<false>(p, tmk, tmv, dtype, pdl, stream);
+}
+
+cudaError_t launch_prefix_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
+                               bool pdl, cudaStream_t stream) {
+  return launch_umma<true>(p, tmk, tmv, dtype, pdl, stream);
 }
 
 }  // namespace pa

@@ -10,8 +10,26 @@
 #pragma once
 
 #include "pa_common.cuh"
+#include "pa_internal.h"
 
 namespace pa {
+
+// Tokens of prefix group gi that the cascade's prefix kernel attends: the
+// group's prefix length within the host bound and the block-table capacity,
+// rounded down to whole 16-token units (the rest is attended per member).
+__device__ __forceinline__ int cascade_prefix_tokens(const DecodeParams& p, int gi) {
+  const int P = min(max(p.group_prefix[gi], 0), min(p.max_prefix, p.max_blocks * p.bs));
+  return P & ~(kUnitTokens - 1);
+}
+
+// Prefix state of one query row (row index ridx): the maximum of its splits'
+// reference maxima (-inf when the row has none) -- the first pass of a
+// log-sum-exp fold over the splits.
+__device__ __forceinline__ float prefix_max(const DecodeParams& p, long long ridx, long long R) {
+  float m = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) m = fmaxf(m, p.pre_ml[s * R + ridx].x);
+  return m;
+}
 
 // Whether P is carried as hi + lo parts in the P.V product (bf16 only).
 template <typename T>
@@ -196,6 +214,61 @@ __device__ __forceinline__ void store_rows(T* op0, T* op1, const float (&o_acc)[
     if (op0) *reinterpret_cast<uint32_t*>(op0 + d) = pack2<T>(o_acc[nd][0] * inv0, o_acc[nd][1] * inv0);
     if (op1) *reinterpret_cast<uint32_t*>(op1 + d) = pack2<T>(o_acc[nd][2] * inv1, o_acc[nd][3] * inv1);
   }
+}
+
+// store_rows for rows that also have a cascade prefix part: the prefix states
+// of query rows ridx0 / ridx1 (one (m, l, acc) per split) are folded into the
+// warp's running (m, l, acc) with a log-sum-exp merge, then normalised.
+// m0 / m1 are the rows' running maxima (log2 domain, -inf when nothing was
+// attended), l0 / l1 their full sums; o_acc is consumed.
+template <typename T, int D>
+__device__ __forceinline__ void store_rows_folded(T* op0, T* op1, float (&o_acc)[D / 8][4], float m0, float m1,
+                                                  float l0, float l1, long long ridx0, long long ridx1,
+                                                  const DecodeParams& p, int quad) {
+  const long long R = (long long)p.B * p.Hq * p.q_len;
+  float M0 = m0, M1 = m1;
+  if (op0) M0 = fmaxf(M0, prefix_max(p, ridx0, R));
+  if (op1) M1 = fmaxf(M1, prefix_max(p, ridx1, R));
+  const float base0 = (M0 == -INFINITY) ? 0.f : M0;
+  const float base1 = (M1 == -INFINITY) ? 0.f : M1;
+  const float w0 = ex2(m0 - base0);
+  const float w1 = ex2(m1 - base1);
+  l0 *= w0;
+  l1 *= w1;
+#pragma unroll
+  for (int nd = 0; nd < D / 8; ++nd) {
+    o_acc[nd][0] *= w0;
+    o_acc[nd][1] *= w0;
+    o_acc[nd][2] *= w1;
+    o_acc[nd][3] *= w1;
+  }
+  for (int s = 0; s < p.splits; ++s) {
+    if (op0) {
+      const float2 ml = __ldcg(&p.pre_ml[s * R + ridx0]);
+      const float ws = ex2(ml.x - base0);
+      l0 += ws * ml.y;
+      const float* a = p.pre_acc + (s * R + ridx0) * D + 2 * quad;
+#pragma unroll
+      for (int nd = 0; nd < D / 8; ++nd) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(a + nd * 8));
+        o_acc[nd][0] = fmaf(ws, v.x, o_acc[nd][0]);
+        o_acc[nd][1] = fmaf(ws, v.y, o_acc[nd][1]);
+      }
+    }
+    if (op1) {
+      const float2 ml = __ldcg(&p.pre_ml[s * R + ridx1]);
+      const float ws = ex2(ml.x - base1);
+      l1 += ws * ml.y;
+      const float* a = p.pre_acc + (s * R + ridx1) * D + 2 * quad;
+#pragma unroll
+      for (int nd = 0; nd < D / 8; ++nd) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(a + nd * 8));
+        o_acc[nd][2] = fmaf(ws, v.x, o_acc[nd][2]);
+        o_acc[nd][3] = fmaf(ws, v.y, o_acc[nd][3]);
+      }
+    }
+  }
+  store_rows<T, D>(op0, op1, o_acc, l0, l1, quad);
 }
 
 }  // namespace pa

@@ -34,7 +34,7 @@ def bucket_max_blocks(max_blocks: int) -> int:
 
 class DecodeStepGraph:
     def __init__(self, key_caches, value_caches, *, batch: int, max_blocks: int, num_q_heads: int,
-                 q_len: int = 1, scale: float, warmup: int = 1):
+                 q_len: int = 1, scale: float, warmup: int = 1, prefix_groups=None):
         if len(key_caches) != len(value_caches) or not key_caches:
             raise ValueError("one key and one value cache view per layer")
         kc0 = key_caches[0]
@@ -45,6 +45,9 @@ class DecodeStepGraph:
         dt = kc0.dtype
         L = len(key_caches)
         self.scale = float(scale)
+        # shared-prefix groups (cascade); their tensors are read at replay, so
+        # they may be rewritten in place between steps (same host bounds)
+        self.prefix_groups = prefix_groups
         self.batch, self.max_blocks, self.q_len = batch, max_blocks, q_len
         dev = self.device
         self.query = [torch.zeros(batch, num_q_heads, q_len, D, dtype=dt, device=dev) for _ in range(L)]
@@ -67,7 +70,7 @@ class DecodeStepGraph:
             paged_attention_decode(
                 self.query[layer], self.key_caches[layer], self.value_caches[layer], self.block_tables,
                 self.context_lens, self.scale, self.slot_mapping, self.new_key[layer], self.new_value[layer],
-                out=self.out[layer],
+                out=self.out[layer], prefix_groups=self.prefix_groups,
             )
 
     def replay(self) -> list[torch.Tensor]:

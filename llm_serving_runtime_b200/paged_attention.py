@@ -63,6 +63,7 @@ class DeviceErrorFlags:
     TABLE_UNDERRUN = _lib.PA_DEVERR_TABLE_UNDERRUN
     SLOT_RANGE = _lib.PA_DEVERR_SLOT_RANGE
     WAIT_TIMEOUT = _lib.PA_DEVERR_WAIT_TIMEOUT
+    PREFIX = _lib.PA_DEVERR_PREFIX
 
 
 def describe_device_errors(flags: int) -> str:
@@ -75,6 +76,8 @@ def describe_device_errors(flags: int) -> str:
         parts.append("slot outside the pool")
     if flags & DeviceErrorFlags.WAIT_TIMEOUT:
         parts.append("bounded wait on a bulk copy timed out")
+    if flags & DeviceErrorFlags.PREFIX:
+        parts.append("prefix group does not match its members' block tables or bounds")
     return "; ".join(parts)
 
 
@@ -277,6 +280,19 @@ def kv_append(
             raise IndexError(describe_device_errors(flags))
 
 
+def _cascade_workspace_bytes(B: int, Hq: int, Hkv: int, q_len: int, D: int, dcode: int, dev_index: int,
+                             groups) -> int:
+    key = (B, Hq, Hkv, q_len, D, dcode, dev_index, groups.num_groups, int(groups.max_members),
+           int(groups.max_prefix_len))
+    n = _ws_bytes_cache.get(key)
+    if n is None:
+        n = _lib.load().pa_cascade_workspace_bytes(B, Hq, Hkv, q_len, D, dcode, dev_index, *key[7:])
+        if n == 0:
+            raise RuntimeError(f"pa_cascade_workspace_bytes failed: {_lib.last_error()}")
+        _ws_bytes_cache[key] = n
+    return n
+
+
 def paged_attention_decode(
     query: torch.Tensor,
     key_cache: torch.Tensor,
@@ -292,8 +308,13 @@ def paged_attention_decode(
     context_lens_include_new: bool = False,
     workspace: torch.Tensor | None = None,
     validate: bool | None = None,
+    prefix_groups=None,
 ) -> torch.Tensor:
-    """Append this step's K/V (optional) and attend; returns [B, Hq, q_len, D]."""
+    """Append this step's K/V (optional) and attend; returns [B, Hq, q_len, D].
+
+    ``prefix_groups`` (a ``prefix_sharing.PrefixGroups``) marks rows whose
+    tables share leading physical blocks: the call then attends each shared
+    block once per group (cascade) and returns the same result."""
     _check_cache_pair(key_cache, value_cache)
     device = key_cache.device
     if query.dim() != 4:
@@ -331,8 +352,15 @@ def paged_attention_decode(
 
     lib = _lib.load()
     dcode = _DTYPE_CODE[query.dtype]
+    cascade = prefix_groups is not None and prefix_groups.num_groups > 0
+    if cascade:
+        if prefix_groups.seq_group.numel() != B or prefix_groups.seq_group.device != device:
+            raise ValueError("prefix_groups must describe this batch on the cache's device")
+        need = _cascade_workspace_bytes(B, Hq, Hkv, q_len, D, dcode, device.index, prefix_groups)
+    else:
+        need = _workspace_bytes(B, Hq, Hkv, q_len, D, dcode, device.index)
     if workspace is None:
-        workspace = decode_workspace(device, _workspace_bytes(B, Hq, Hkv, q_len, D, dcode, device.index))
+        workspace = decode_workspace(device, need)
 
     appended = False
     if key is not None:
@@ -364,7 +392,12 @@ def paged_attention_decode(
     args.workspace_bytes = workspace.numel()
     args.allow_overlap_with_previous = 1 if appended else 0
     with _with_device(device):
-        _lib.check(lib.pa_decode(ctypes.byref(args), _stream_ptr(device)), "pa_decode")
+        if cascade:
+            groups = prefix_groups.to_args()
+            _lib.check(lib.pa_decode_cascade(ctypes.byref(args), ctypes.byref(groups), _stream_ptr(device)),
+                       "pa_decode_cascade")
+        else:
+            _lib.check(lib.pa_decode(ctypes.byref(args), _stream_ptr(device)), "pa_decode")
     if validate if validate is not None else _VALIDATE_DEFAULT:
         flags = read_device_errors(workspace=workspace)
         if flags:

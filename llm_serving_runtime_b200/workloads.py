@@ -106,6 +106,21 @@ class DecodeWorkload:
     def attended_lengths(self) -> torch.Tensor:
         return self.context_lens.to(torch.int64).cpu() + self.q_len
 
+    def shared_prefixes(self):
+        """The workload's prefix groups (``PrefixGroups``) on its device, or None."""
+        spec = self.spec
+        if not spec.prefix_groups:
+            return None
+        from .prefix_sharing import PrefixGroups
+
+        per_group = spec.batch // spec.prefix_groups
+        members: dict[int, list[int]] = {}
+        for i, r in enumerate(self.rows):
+            members.setdefault(r // per_group, []).append(i)
+        groups = [members[k] for k in sorted(members)]
+        return PrefixGroups.from_members(groups, [spec.prefix_tokens] * len(groups), self.batch,
+                                         self.query.device)
+
     def to(self, device: str | torch.device) -> "DecodeWorkload":
         """Copy every tensor to ``device`` (bit-identical inputs on CPU and GPU)."""
         names = ("query", "key_cache", "value_cache", "block_tables", "context_lens",

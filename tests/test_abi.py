@@ -52,6 +52,8 @@ int main(void) {
   F(pa_decode_args, key_cache) F(pa_decode_args, block_tables) F(pa_decode_args, context_lens)
   F(pa_decode_args, out) F(pa_decode_args, batch) F(pa_decode_args, scale) F(pa_decode_args, workspace)
   F(pa_decode_args, workspace_bytes) F(pa_decode_args, allow_overlap_with_previous)
+  printf("pa_prefix_groups %zu\n", sizeof(pa_prefix_groups));
+  F(pa_prefix_groups, max_prefix_len) F(pa_prefix_groups, member_offsets) F(pa_prefix_groups, seq_group)
   return 0;
 }
 """
@@ -67,11 +69,14 @@ def test_ctypes_structs_match_header_layout(tmp_path):
     assert int(c["pa_cache_view"]) == ctypes.sizeof(_lib.CacheView)
     assert int(c["pa_kv_append_args"]) == ctypes.sizeof(_lib.KvAppendArgs)
     assert int(c["pa_decode_args"]) == ctypes.sizeof(_lib.DecodeArgs)
+    assert int(c["pa_prefix_groups"]) == ctypes.sizeof(_lib.PrefixGroupsArgs)
+    classes = {"pa_kv_append_args": _lib.KvAppendArgs, "pa_decode_args": _lib.DecodeArgs,
+               "pa_prefix_groups": _lib.PrefixGroupsArgs}
     for key, val in c.items():
         if "." not in key:
             continue
         struct, field = key.split(".")
-        cls = _lib.KvAppendArgs if struct == "pa_kv_append_args" else _lib.DecodeArgs
+        cls = classes[struct]
         assert getattr(cls, field).offset == int(val), key
 
 
@@ -93,6 +98,18 @@ def test_null_arguments_are_rejected_without_a_gpu():
         _lib.check(_lib.PA_ERR_DEVICE, "pa_decode")
     with pytest.raises(RuntimeError):
         _lib.check(_lib.PA_ERR_WORKSPACE, "pa_decode")
+
+
+def test_cascade_argument_errors_without_a_gpu():
+    lib = _lib.load()
+    args = _lib.DecodeArgs()
+    assert lib.pa_decode_cascade(ctypes.byref(args), None, None) == _lib.PA_ERR_INVALID_ARGUMENT
+    groups = _lib.PrefixGroupsArgs()
+    groups.num_groups = 2
+    assert lib.pa_decode_cascade(ctypes.byref(args), ctypes.byref(groups), None) == _lib.PA_ERR_INVALID_ARGUMENT
+    assert "member_offsets" in _lib.last_error()
+    groups.num_groups = -1
+    assert lib.pa_decode_cascade(ctypes.byref(args), ctypes.byref(groups), None) == _lib.PA_ERR_INVALID_ARGUMENT
 
 
 def test_empty_batch_is_a_no_op():

@@ -156,7 +156,7 @@ size_t workspace_bytes_impl(int slot_rows, int D, int nw_total) {
 // reach one CTA per SM, at most 16.
 struct CascadeShape {
   int splits, split_tokens;
-  size_t ml_bytes, acc_bytes;
+  size_t ml_bytes, acc_bytes, cnt_bytes;
 };
 
 CascadeShape cascade_shape(int num_sms, int num_groups, int max_members, int max_prefix, int Hkv, int GQ,
@@ -177,6 +177,7 @@ CascadeShape cascade_shape(int num_sms, int num_groups, int max_members, int max
   c.splits = std::max(1, (prefix + per - 1) / per);
   c.ml_bytes = round_up((size_t)c.splits * rows * 8);
   c.acc_bytes = round_up((size_t)c.splits * rows * D * 4);
+  c.cnt_bytes = round_up((size_t)tiles * 4);
   return c;
 }
 
@@ -308,7 +309,7 @@ size_t pa_cascade_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t nu
   const DecodeShape s = decode_shape(num_q_heads, num_kv_heads, q_len);
   const CascadeShape c = cascade_shape(info->num_sms, num_groups, max_members, max_prefix_len, num_kv_heads, s.GQ,
                                        (long long)batch * num_q_heads * q_len, head_dim);
-  return base + c.ml_bytes + c.acc_bytes;
+  return base + c.ml_bytes + c.acc_bytes + c.cnt_bytes;
 }
 
 static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, void* stream);
@@ -436,7 +437,7 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, voi
   // query rows; without them the plain decode computes the same result.
   const bool cascade = grp != nullptr && q_rows16;
   size_t need = workspace_bytes_impl(p.slot_rows, D, p.nw_total);
-  CascadeShape cs = {1, pa::kUmmaChunkTokens, 0, 0};
+  CascadeShape cs = {1, pa::kUmmaChunkTokens, 0, 0, 0};
   if (cascade) {
     if ((long long)grp->max_members * s.GQ > (1LL << 30))
       return fail(PA_ERR_UNSUPPORTED, "max_members * rows per kv head too large");
@@ -444,7 +445,7 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, voi
                        (long long)p.B * p.Hq * p.q_len, D);
   }
   const size_t decode_need = need;
-  need += cs.ml_bytes + cs.acc_bytes;
+  need += cs.ml_bytes + cs.acc_bytes + cs.cnt_bytes;
   if (a->workspace_bytes < need)
     return fail(PA_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", a->workspace_bytes, need);
   char* ws = static_cast<char*>(a->workspace);
@@ -457,6 +458,7 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, voi
     p.member_seq = grp->member_seqs;
     p.pre_ml = reinterpret_cast<float2*>(ws + decode_need);
     p.pre_acc = reinterpret_cast<float*>(ws + decode_need + cs.ml_bytes);
+    p.pre_cnt = reinterpret_cast<int32_t*>(ws + decode_need + cs.ml_bytes + cs.acc_bytes);
     p.num_groups = grp->num_groups;
     p.max_members = grp->max_members;
     p.max_prefix = grp->max_prefix_len;
@@ -497,7 +499,15 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, voi
     // Prefix pass (tcgen05), then the decode kernel over each member's own
     // tokens, which folds the prefix states in; it waits for the prefix grid.
     g_last_kernel = "pa::prefill_umma_kernel<prefix> + pa::decode_mma_kernel";
-    e = pa::launch_prefix_umma(p, tmk, tmv, dtype, pdl, strm);
+    bool prefix_pdl = pdl;
+    if (cs.splits > 1) {
+      // The split arrival counters sit after the shape-dependent regions, which
+      // calls of other shapes reuse: start them at zero.
+      e = cudaMemsetAsync(p.pre_cnt, 0, cs.cnt_bytes, strm);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(prefix split counters)");
+      prefix_pdl = false;  // the previous operation on the stream is now the memset
+    }
+    e = pa::launch_prefix_umma(p, tmk, tmv, dtype, prefix_pdl, strm);
     if (e != cudaSuccess) return cuda_fail(e, "cascade prefix launch");
     e = pa::launch_decode_mma(p, tmk, tmv, dtype, grid, smem, true, strm);
     if (e != cudaSuccess) return cuda_fail(e, "decode launch");

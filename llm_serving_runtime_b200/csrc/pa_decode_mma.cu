@@ -56,7 +56,9 @@ __device__ __forceinline__ int group_units(int L, int mg, const DecodeParams& p)
   return lim < 0 ? 0 : (lim + kUnitTokens) / kUnitTokens;
 }
 
-template <typename T, int D>
+// kCascade: the call carries shared-prefix groups (pa_decode_cascade); each
+// member's prefix units are skipped and the prefix states folded into its rows.
+template <typename T, int D, bool kCascade>
 __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                       const DecodeParams p) {
@@ -79,7 +81,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   // Cascade (shared prefixes): the prefix kernel has attended each member's
   // first s_u0[b] units; the work list starts every sequence after them.
   int* s_u0 = s_pref + p.B + 1;
-  const bool cascade = p.seq_group != nullptr;
+  constexpr bool cascade = kCascade;
   __shared__ int s_warp_tot[kDecodeWarps];
 
   const int tid = threadIdx.x;
@@ -153,7 +155,6 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   // Row groups with nothing to attend get no unit: their rows are zero, or,
   // under the cascade, the normalised prefix part alone.
   auto fill_empty_rows = [&]() {
-    const long long R = (long long)B * p.Hq * p.q_len;
     for (int b = blockIdx.x; b < B; b += gridDim.x) {
       const bool pre = cascade && s_u0[b] > 0;
       for (int mg = 0; mg < p.NMG; ++mg) {
@@ -168,33 +169,24 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           T* o = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
                  (long long)t * p.o_st + 2 * d2;
           uint32_t v = 0u;
-          if (pre) {
+          if (pre) {  // merged prefix state: out = acc / l
             const long long ridx = ((long long)b * p.Hq + h * p.G + g) * p.q_len + t;
-            const float M = prefix_max(p, ridx, R);
-            const float base = (M == -INFINITY) ? 0.f : M;
-            float lsum = 0.f, a0 = 0.f, a1 = 0.f;
-            for (int s = 0; s < p.splits; ++s) {
-              const float2 ml = __ldcg(&p.pre_ml[s * R + ridx]);
-              const float w = ex2(ml.x - base);
-              const float2 a = __ldcg(reinterpret_cast<const float2*>(p.pre_acc + (s * R + ridx) * D + 2 * d2));
-              lsum += w * ml.y;
-              a0 = fmaf(w, a.x, a0);
-              a1 = fmaf(w, a.y, a1);
-            }
+            const float lsum = __ldcg(&p.pre_ml[ridx]).y;
+            const float2 a = __ldcg(reinterpret_cast<const float2*>(p.pre_acc + ridx * D + 2 * d2));
             const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-            v = pack2<T>(a0 * inv, a1 * inv);
+            v = pack2<T>(a.x * inv, a.y * inv);
           }
           *reinterpret_cast<uint32_t*>(o) = v;
         }
       }
     }
   };
-  if (!cascade) fill_empty_rows();
+  if constexpr (!cascade) fill_empty_rows();
 
   // Everything below reads the KV cache, which the previous kernel may write
   // (and, under the cascade, the prefix states the previous kernel leaves).
   pdl_wait_previous();
-  if (cascade) fill_empty_rows();
+  if constexpr (cascade) fill_empty_rows();
 
   const long long W = s_pref[B];
   if (W == 0) return;
@@ -557,22 +549,17 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
                 const int qr = mg * 16 + rg + r;
                 const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
                 if (cascade && s_u0[b] > 0) {
-                  // fold the row's prefix part (one (m, l, acc) per split)
-                  const long long R = (long long)B * p.Hq * p.q_len;
+                  // fold the row's merged prefix state (loads issued together)
                   const long long ridx = ((long long)b * p.Hq + h * p.G + g) * p.q_len + t;
-                  const float M2 = fmaxf(M[r], prefix_max(p, ridx, R));
-                  const float c = ex2(M[r] - M2);
-                  lsum[r] *= c;
+                  const float2 ml = __ldcg(&p.pre_ml[ridx]);
+                  float pa[DPL];
 #pragma unroll
-                  for (int k = 0; k < DPL; ++k) acc[r][k] *= c;
-                  for (int s = 0; s < p.splits; ++s) {
-                    const float2 ml = __ldcg(&p.pre_ml[s * R + ridx]);
-                    const float w = ex2(ml.x - M2);
-                    lsum[r] += w * ml.y;
-                    const float* a = p.pre_acc + (s * R + ridx) * D;
+                  for (int k = 0; k < DPL; ++k) pa[k] = __ldcg(p.pre_acc + ridx * D + lane + 32 * k);
+                  const float M2 = fmaxf(M[r], ml.x);
+                  const float c = ex2(M[r] - M2), w = ex2(ml.x - M2);
+                  lsum[r] = fmaf(lsum[r], c, w * ml.y);
 #pragma unroll
-                    for (int k = 0; k < DPL; ++k) acc[r][k] = fmaf(w, __ldcg(a + lane + 32 * k), acc[r][k]);
-                  }
+                  for (int k = 0; k < DPL; ++k) acc[r][k] = fmaf(acc[r][k], c, w * pa[k]);
                 }
                 const float inv = lsum[r] > 0.f ? 1.f / lsum[r] : 0.f;
                 T* op = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
@@ -599,7 +586,7 @@ size_t decode_mma_smem_bytes(int D, int B, int stages, bool cascade) {
          (size_t)((cascade ? 3 : 2) * B + 1) * 4;
 }
 
-template <typename T, int D>
+template <typename T, int D, bool kCascade>
 static cudaError_t launch_mma_impl(const DecodeParams& p, const CUtensorMap& tmk,
                                    const CUtensorMap& tmv, int grid, size_t smem, bool pdl,
                                    cudaStream_t stream) {
@@ -613,29 +600,42 @@ static cudaError_t launch_mma_impl(const DecodeParams& p, const CUtensorMap& tmk
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = pdl ? attr : nullptr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<T, D>, tmk, tmv, p);
+  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<T, D, kCascade>, tmk, tmv, p);
 }
 
-cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
-                              int dtype, int grid, size_t smem, bool pdl, cudaStream_t stream) {
+template <bool kCascade>
+static cudaError_t launch_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
+                              int grid, size_t smem, bool pdl, cudaStream_t stream) {
   if (dtype == PA_DTYPE_BFLOAT16) {
-    if (p.D == 128) return launch_mma_impl<__nv_bfloat16, 128>(p, tmk, tmv, grid, smem, pdl, stream);
-    if (p.D == 64) return launch_mma_impl<__nv_bfloat16, 64>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 128) return launch_mma_impl<__nv_bfloat16, 128, kCascade>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 64) return launch_mma_impl<__nv_bfloat16, 64, kCascade>(p, tmk, tmv, grid, smem, pdl, stream);
   } else if (dtype == PA_DTYPE_FLOAT16) {
-    if (p.D == 128) return launch_mma_impl<__half, 128>(p, tmk, tmv, grid, smem, pdl, stream);
-    if (p.D == 64) return launch_mma_impl<__half, 64>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 128) return launch_mma_impl<__half, 128, kCascade>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 64) return launch_mma_impl<__half, 64, kCascade>(p, tmk, tmv, grid, smem, pdl, stream);
   }
   return cudaErrorInvalidValue;
 }
 
-cudaError_t decode_mma_prepare(int dtype, int D, size_t smem) {
-  const void* fn = nullptr;
+cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                              int dtype, int grid, size_t smem, bool pdl, cudaStream_t stream) {
+  return p.seq_group != nullptr ? launch_mma<true>(p, tmk, tmv, dtype, grid, smem, pdl, stream)
+                                : launch_mma<false>(p, tmk, tmv, dtype, grid, smem, pdl, stream);
+}
+
+template <bool kCascade>
+static const void* decode_fn(int dtype, int D) {
   if (dtype == PA_DTYPE_BFLOAT16)
-    fn = D == 128 ? (const void*)decode_mma_kernel<__nv_bfloat16, 128>
-                  : (const void*)decode_mma_kernel<__nv_bfloat16, 64>;
-  else
-    fn = D == 128 ? (const void*)decode_mma_kernel<__half, 128> : (const void*)decode_mma_kernel<__half, 64>;
-  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return D == 128 ? (const void*)decode_mma_kernel<__nv_bfloat16, 128, kCascade>
+                    : (const void*)decode_mma_kernel<__nv_bfloat16, 64, kCascade>;
+  return D == 128 ? (const void*)decode_mma_kernel<__half, 128, kCascade>
+                  : (const void*)decode_mma_kernel<__half, 64, kCascade>;
+}
+
+cudaError_t decode_mma_prepare(int dtype, int D, size_t smem) {
+  cudaError_t e = cudaFuncSetAttribute(decode_fn<false>(dtype, D), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(decode_fn<true>(dtype, D), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
 }  // namespace pa

@@ -56,14 +56,16 @@ struct DecodeParams {
   // P_g = prefix_lens[g] rounded down to whole 16-token units, in `splits`
   // ranges of split_tokens, and leaves per split and query row (b, hq, t)
   // (m, l) in pre_ml and the unnormalised accumulator in pre_acc, at row index
-  // (b * Hq + hq) * q_len + t.  The decode kernel starts each member at P_g
-  // and folds those states into its rows.
+  // (b * Hq + hq) * q_len + t; the last split of a tile to finish merges all
+  // splits into split 0.  The decode kernel starts each member at P_g and
+  // folds that one state into its rows.
   const int32_t* seq_group;     // [B] group of each row, -1: none
   const int32_t* group_prefix;  // [num_groups] shared tokens
   const int32_t* member_off;    // [num_groups + 1]
   const int32_t* member_seq;    // member rows
-  float2* pre_ml;               // [splits][B * Hq * q_len]
+  float2* pre_ml;               // [splits][B * Hq * q_len]; split 0 ends up holding the merged state
   float* pre_acc;               // [splits][B * Hq * q_len][D]
+  int32_t* pre_cnt;             // [num_groups * Hkv * tiles] split arrival counters (zeroed per call)
   int32_t num_groups, max_members, max_prefix, splits, split_tokens;
 };
 

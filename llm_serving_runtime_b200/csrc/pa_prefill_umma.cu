@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   // row, the rows that exist, and the token range [kv_lo, kv_end) streamed in
   // n_chunks chunks (tokens at or past kv_end are never attended).
   int b_kv, h, row0, rows_total, kv_lo, kv_end, n_chunks;
-  int moff = 0, split = 0, prefix_tokens = 0;
+  int moff = 0, split = 0, prefix_tokens = 0, tile_id = 0;
   if constexpr (kPrefix) {
     const int MT = (p.max_members * p.GQ + 127) / 128;
     int idx = (int)blockIdx.x;
@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     idx /= p.Hkv;
     const int gi = idx % p.num_groups;
     split = idx / p.num_groups;
+    tile_id = (gi * p.Hkv + h) * MT + mt;
     moff = p.member_off[gi];
     int nmem = p.member_off[gi + 1] - moff;
     if (nmem > p.max_members || p.group_prefix[gi] > p.max_prefix) {
@@ -569,6 +570,52 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
               v = make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]),
                               __uint_as_float(o[i + 3]));
             *reinterpret_cast<float4*>(arow + c0 + i) = v;
+          }
+        }
+      }
+      if (p.splits > 1) {
+        // The last split of this tile to finish merges every split's state of
+        // its rows into split 0 (log-sum-exp), so the decode kernel folds one
+        // state per row.
+        __shared__ int s_last;
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
+        if (tid == 0) s_last = atomicAdd(&p.pre_cnt[tile_id], 1) == p.splits - 1;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (s_last) {
+          __threadfence();
+          const long long R = (long long)p.B * p.Hq * p.q_len;
+          const long long r0 = ridx - (long long)split * R;  // this row in split 0
+          if (row_ok) {
+            float M = -INFINITY;
+            for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(&p.pre_ml[sp * R + r0]).x);
+            const float base = (M == -INFINITY) ? 0.f : M;
+            float lsum = 0.f;
+            for (int sp = 0; sp < p.splits; ++sp) {
+              const float2 ml = __ldcg(&p.pre_ml[sp * R + r0]);
+              lsum += ex2(ml.x - base) * ml.y;
+            }
+            for (int c0 = 0; c0 < D; c0 += 32) {
+              float4 a[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int sp = 0; sp < p.splits; ++sp) {
+                const float w = ex2(__ldcg(&p.pre_ml[sp * R + r0]).x - base);
+                const float4* src = reinterpret_cast<const float4*>(p.pre_acc + (sp * R + r0) * D + c0);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const float4 v = __ldcg(src + i);
+                  a[i].x = fmaf(w, v.x, a[i].x);
+                  a[i].y = fmaf(w, v.y, a[i].y);
+                  a[i].z = fmaf(w, v.z, a[i].z);
+                  a[i].w = fmaf(w, v.w, a[i].w);
+                }
+              }
+              float4* dst = reinterpret_cast<float4*>(p.pre_acc + r0 * D + c0);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) dst[i] = a[i];
+            }
+            p.pre_ml[r0] = make_float2(M, lsum);
           }
         }
       }

@@ -22,14 +22,6 @@ __device__ __forceinline__ int cascade_prefix_tokens(const DecodeParams& p, int 
   return P & ~(kUnitTokens - 1);
 }
 
-// Prefix state of one query row (row index ridx): the maximum of its splits'
-// reference maxima (-inf when the row has none) -- the first pass of a
-// log-sum-exp fold over the splits.
-__device__ __forceinline__ float prefix_max(const DecodeParams& p, long long ridx, long long R) {
-  float m = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) m = fmaxf(m, p.pre_ml[s * R + ridx].x);
-  return m;
-}
 
 // Whether P is carried as hi + lo parts in the P.V product (bf16 only).
 template <typename T>
@@ -216,57 +208,35 @@ __device__ __forceinline__ void store_rows(T* op0, T* op1, const float (&o_acc)[
   }
 }
 
-// store_rows for rows that also have a cascade prefix part: the prefix states
-// of query rows ridx0 / ridx1 (one (m, l, acc) per split) are folded into the
-// warp's running (m, l, acc) with a log-sum-exp merge, then normalised.
-// m0 / m1 are the rows' running maxima (log2 domain, -inf when nothing was
-// attended), l0 / l1 their full sums; o_acc is consumed.
+// store_rows for rows that also have a cascade prefix part: the prefix state
+// of query rows ridx0 / ridx1 ((m, l) and the unnormalised accumulator, all
+// splits already merged) is folded into the warp's running (m, l, acc) with a
+// log-sum-exp merge, then normalised.  m0 / m1 are the rows' running maxima
+// (log2 domain, -inf when nothing was attended), l0 / l1 their full sums;
+// o_acc is consumed.
 template <typename T, int D>
 __device__ __forceinline__ void store_rows_folded(T* op0, T* op1, float (&o_acc)[D / 8][4], float m0, float m1,
                                                   float l0, float l1, long long ridx0, long long ridx1,
                                                   const DecodeParams& p, int quad) {
-  const long long R = (long long)p.B * p.Hq * p.q_len;
-  float M0 = m0, M1 = m1;
-  if (op0) M0 = fmaxf(M0, prefix_max(p, ridx0, R));
-  if (op1) M1 = fmaxf(M1, prefix_max(p, ridx1, R));
+  const float2 ml0 = op0 ? __ldcg(&p.pre_ml[ridx0]) : make_float2(-INFINITY, 0.f);
+  const float2 ml1 = op1 ? __ldcg(&p.pre_ml[ridx1]) : make_float2(-INFINITY, 0.f);
+  const float M0 = fmaxf(m0, ml0.x), M1 = fmaxf(m1, ml1.x);
   const float base0 = (M0 == -INFINITY) ? 0.f : M0;
   const float base1 = (M1 == -INFINITY) ? 0.f : M1;
-  const float w0 = ex2(m0 - base0);
-  const float w1 = ex2(m1 - base1);
-  l0 *= w0;
-  l1 *= w1;
+  const float w0 = ex2(m0 - base0), w1 = ex2(m1 - base1);      // this warp's part
+  const float v0 = ex2(ml0.x - base0), v1 = ex2(ml1.x - base1);  // the prefix part
+  l0 = fmaf(l0, w0, v0 * ml0.y);
+  l1 = fmaf(l1, w1, v1 * ml1.y);
+  const float* a0 = p.pre_acc + ridx0 * D + 2 * quad;
+  const float* a1 = p.pre_acc + ridx1 * D + 2 * quad;
 #pragma unroll
   for (int nd = 0; nd < D / 8; ++nd) {
-    o_acc[nd][0] *= w0;
-    o_acc[nd][1] *= w0;
-    o_acc[nd][2] *= w1;
-    o_acc[nd][3] *= w1;
-  }
-  for (int s = 0; s < p.splits; ++s) {
-    if (op0) {
-      const float2 ml = __ldcg(&p.pre_ml[s * R + ridx0]);
-      const float ws = ex2(ml.x - base0);
-      l0 += ws * ml.y;
-      const float* a = p.pre_acc + (s * R + ridx0) * D + 2 * quad;
-#pragma unroll
-      for (int nd = 0; nd < D / 8; ++nd) {
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(a + nd * 8));
-        o_acc[nd][0] = fmaf(ws, v.x, o_acc[nd][0]);
-        o_acc[nd][1] = fmaf(ws, v.y, o_acc[nd][1]);
-      }
-    }
-    if (op1) {
-      const float2 ml = __ldcg(&p.pre_ml[s * R + ridx1]);
-      const float ws = ex2(ml.x - base1);
-      l1 += ws * ml.y;
-      const float* a = p.pre_acc + (s * R + ridx1) * D + 2 * quad;
-#pragma unroll
-      for (int nd = 0; nd < D / 8; ++nd) {
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(a + nd * 8));
-        o_acc[nd][2] = fmaf(ws, v.x, o_acc[nd][2]);
-        o_acc[nd][3] = fmaf(ws, v.y, o_acc[nd][3]);
-      }
-    }
+    const float2 x0 = op0 ? __ldcg(reinterpret_cast<const float2*>(a0 + nd * 8)) : make_float2(0.f, 0.f);
+    const float2 x1 = op1 ? __ldcg(reinterpret_cast<const float2*>(a1 + nd * 8)) : make_float2(0.f, 0.f);
+    o_acc[nd][0] = fmaf(o_acc[nd][0], w0, v0 * x0.x);
+    o_acc[nd][1] = fmaf(o_acc[nd][1], w0, v0 * x0.y);
+    o_acc[nd][2] = fmaf(o_acc[nd][2], w1, v1 * x1.x);
+    o_acc[nd][3] = fmaf(o_acc[nd][3], w1, v1 * x1.y);
   }
   store_rows<T, D>(op0, op1, o_acc, l0, l1, quad);
 }

@@ -162,7 +162,8 @@ struct CascadeShape {
 CascadeShape cascade_shape(int num_sms, int num_groups, int max_members, int max_prefix, int Hkv, int GQ,
                            long long rows, int D) {
   CascadeShape c;
-  const long long tiles = (long long)num_groups * Hkv * (((long long)max_members * GQ + 127) / 128);
+  // prefix-pass CTAs per split: 256 member rows each
+  const long long tiles = (long long)num_groups * Hkv * (((long long)max_members * GQ + 255) / 256);
   const int chunk = pa::kUmmaChunkTokens;
   const int prefix = max_prefix > 0 ? max_prefix : 0;
   int splits = 1;

@@ -3,25 +3,31 @@
 //
 // Same contract and row layout as the other decode kernels: rows of one KV head
 // are token-major (row r = query token r / G of head h*G + r % G); query token t
-// attends positions 0 .. L - q_len + t.  A CTA owns a 128-row tile of one
-// (sequence, kv head) and streams the sequence's K/V in 64-token chunks:
+// attends positions 0 .. L - q_len + t.  A CTA owns 256 rows -- two 128-row
+// MMA tiles -- of one (sequence, kv head) and streams the sequence's K/V in
+// 64-token chunks shared by both tiles:
 //
-//   warp 4 (producer)  TMA-loads each chunk's four 16-token units (K and V, two
-//                      64-column halves each, 128-byte swizzle) into a 3-stage ring;
-//   warp 5 (MMA)       one thread issues S = Q K^T (M=128, N=64, K=D) into a
-//                      double-buffered TMEM S, and O += P V (M=128, N=D, K=64)
-//                      into TMEM O, signalling mbarriers with tcgen05.commit;
-//   warps 0-3 (softmax) thread i owns query row i = TMEM lane i: it loads its S
-//                      row (tcgen05.ld), masks, takes the max and exponentials
-//                      without any cross-thread reduction, writes its P row
-//                      (bf16: hi and lo parts, so P.V keeps ~16 bits of P) into
-//                      swizzled shared memory as the A operand of the PV MMA,
-//                      and finally reads O back, normalises and stores it.
+//   warp 8 (producer)   TMA-loads each chunk's four 16-token units (K and V, two
+//                       64-column halves each, 128-byte swizzle) into a ring;
+//   warp 9 (MMA)        one thread issues, per chunk, S_t = Q_t K^T (M=128, N=64,
+//                       K=D) for both tiles into TMEM, then O_t += P_t V
+//                       (M=128, N=D, K=64) with P_t read from TMEM, signalling
+//                       mbarriers with tcgen05.commit;
+//   warps 0-3 / 4-7     softmax of tile 0 / tile 1: thread i owns query row i
+//                       = TMEM lane i; it loads its S row (tcgen05.ld), masks,
+//                       takes the max and exponentials without any cross-thread
+//                       reduction, and writes its P row (bf16: hi and lo parts,
+//                       so P.V keeps ~16 bits of P) back over the same TMEM
+//                       columns (tcgen05.st) as the A operand of the PV MMA;
+//                       finally it reads O back, normalises and stores it.
 //
-// The online softmax keeps a reference max per row and rescales O (TMEM load,
-// scale, store) only when a chunk raises the row max by more than 2^8, so p
-// stays below 256 and the arithmetic is exact; most chunks skip the rescale.
-// Every wait is bounded; TMEM is always released before the CTA exits.
+// While one tile's softmax runs, the tensor core works on the other tile's
+// products, so neither waits for the other.  Each tile has two S/P buffers in
+// TMEM; the MMA thread refills a buffer only after the PV that read its P has
+// completed.  The online softmax keeps a reference max per row and rescales O
+// (TMEM load, scale, store) only when a chunk raises the row max by more than
+// 2^8, so p stays below 256 and the arithmetic is exact; most chunks skip the
+// rescale.  Every wait is bounded; TMEM is always released before the CTA exits.
 #include <math.h>
 
 #include "pa_common.cuh"
@@ -32,10 +38,16 @@ namespace pa {
 
 namespace {
 
-constexpr int kChunk = 64;             // tokens per chunk (N of the QK^T MMA)
-constexpr int kUmmaStages = 3;         // K/V chunks in flight
-constexpr uint32_t kTmemCols = 256;    // S double buffer (2 x 64) + O (<= 128)
-constexpr float kRescaleThreshold = 8.f;  // log2 units: rescale when the max grows by > 2^8
+constexpr int kChunk = kUmmaChunkTokens;  // tokens per chunk (N of the QK^T MMA)
+constexpr uint32_t kTmemCols = 512;        // per tile: S/P buffers (2 x 64) + O (<= 128), at column 256 * tile
+constexpr int kTileRows = 256;             // query rows per CTA (two 128-row MMA tiles)
+constexpr float kRescaleThreshold = 8.f;   // log2 units: rescale when the max grows by > 2^8
+
+// K/V chunks in flight: as many as the shared memory left after Q allows.
+template <int D>
+struct kUmmaStages {
+  static constexpr int value = D == 128 ? 4 : 8;
+};
 
 // UMMA A/B element format code of kind::f16: 0 = fp16, 1 = bf16.
 template <typename T>
@@ -74,6 +86,17 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       : "memory");
 }
 
+// Same with the A operand (M x K, K-major: row m in TMEM lane m, two 16-bit
+// elements per 32-bit column) read from tensor memory.
+__device__ __forceinline__ void umma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
@@ -104,6 +127,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -112,51 +141,50 @@ __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) { return (uint32_t
 
 }  // namespace
 
-// kPrefix = false: a CTA owns a 128-row tile of one (sequence, kv head) and
-// writes normalised output rows.  kPrefix = true (the prefix part of
-// pa_decode_cascade): a CTA owns a 128-row tile of the member rows of one
-// (split, prefix group, kv head) -- row r is row r % GQ of member r / GQ --
-// attends the group's shared blocks in the split's token range through the
-// first member's block table, and leaves (m, l, unnormalised O) per row.
+// kPrefix = false: a CTA owns 256 rows of one (sequence, kv head) and writes
+// normalised output rows.  kPrefix = true (the prefix part of
+// pa_decode_cascade): a CTA owns 256 of the member rows of one (split, prefix
+// group, kv head) -- row r is row r % GQ of member r / GQ -- attends the
+// group's shared blocks in the split's token range through the first member's
+// block table, and leaves (m, l, unnormalised O) per row.
 template <typename T, int D, bool kPrefix>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
     prefill_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                         const DecodeParams p) {
   constexpr int HALVES = D / 64;
+  constexpr int S = kUmmaStages<D>::value;
   constexpr uint32_t HALF_BYTES = kChunk * 128;          // 64 rows x 128 B
   constexpr uint32_t KV_BYTES = 2 * HALVES * HALF_BYTES;  // K and V of one chunk
-  constexpr uint32_t Q_BYTES = HALVES * 128 * 128;        // 128 rows x D
-  constexpr uint32_t P_BYTES = 128 * 128;                 // 128 rows x 64 tokens (16-bit)
+  constexpr uint32_t QT_BYTES = HALVES * 128 * 128;       // one 128-row tile of Q
   constexpr bool kSplit = kSplitProbabilities<T>::value;
   constexpr uint32_t FMT = kUmmaFormat<T>::value;
-  const int S = kUmmaStages;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  uint8_t* s_kv = smem;                                 // [stage][K halves | V halves]
-  uint8_t* s_q = s_kv + S * KV_BYTES;                   // [halves][128 rows x 128 B]
-  uint8_t* s_p = s_q + Q_BYTES;                         // [buffer 0/1][hi | lo] 16 KB each
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_p + 4 * P_BYTES);
-  uint64_t* kv_full = bars;                             // [S]
-  uint64_t* kv_empty = kv_full + S;                     // [S]
-  uint64_t* s_full = kv_empty + S;                      // [2]
-  uint64_t* s_free = s_full + 2;                        // [2]
-  uint64_t* p_full = s_free + 2;                        // [2]
-  uint64_t* pv_done = p_full + 2;                       // [2]
-  uint64_t* q_ready = pv_done + 2;                      // [1]
+  uint8_t* s_kv = smem;                  // [stage][K halves | V halves]
+  uint8_t* s_q = s_kv + S * KV_BYTES;    // [tile][halves][128 rows x 128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_q + 2 * QT_BYTES);
+  uint64_t* kv_full = bars;              // [S]
+  uint64_t* kv_empty = kv_full + S;      // [S]
+  uint64_t* s_full = kv_empty + S;       // [tile * 2 + buffer]: S of a chunk is in TMEM
+  uint64_t* p_full = s_full + 4;         // [tile * 2 + buffer]: P of a chunk is in TMEM
+  uint64_t* pv_done = p_full + 4;        // [tile * 2 + buffer]: the PV reading that P completed
+  uint64_t* q_ready = pv_done + 4;       // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+  __shared__ int s_last;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+
   const int cap = p.max_blocks * p.bs;
-  // Tile: the sequence whose block table is read (b_kv), the kv head, the first
+  // CTA: the sequence whose block table is read (b_kv), the kv head, the first
   // row, the rows that exist, and the token range [kv_lo, kv_end) streamed in
   // n_chunks chunks (tokens at or past kv_end are never attended).
   int b_kv, h, row0, rows_total, kv_lo, kv_end, n_chunks;
   int moff = 0, split = 0, prefix_tokens = 0, tile_id = 0;
   if constexpr (kPrefix) {
-    const int MT = (p.max_members * p.GQ + 127) / 128;
+    const int MT = (p.max_members * p.GQ + kTileRows - 1) / kTileRows;
     int idx = (int)blockIdx.x;
     const int mt = idx % MT;
     idx /= MT;
@@ -174,7 +202,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     if (nmem < 0) nmem = 0;
     prefix_tokens = cascade_prefix_tokens(p, gi);
     rows_total = nmem * p.GQ;
-    row0 = mt * 128;
+    row0 = mt * kTileRows;
     kv_lo = split * p.split_tokens;
     kv_end = min(prefix_tokens, kv_lo + p.split_tokens);
     b_kv = nmem > 0 ? p.member_seq[moff] : 0;
@@ -186,8 +214,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     n_chunks = (row0 < rows_total && kv_end > kv_lo) ? (kv_end - kv_lo + kChunk - 1) / kChunk : 0;
   } else {
     const int BH = p.B * p.Hkv;
-    const int MT = (p.GQ + 127) / 128;
-    const int mt = MT - 1 - (int)(blockIdx.x / BH);  // latest (heaviest) tiles first
+    const int MT = (p.GQ + kTileRows - 1) / kTileRows;
+    const int mt = MT - 1 - (int)(blockIdx.x / BH);  // latest (heaviest) row blocks first
     const int bh = (int)(blockIdx.x % BH);
     b_kv = bh / p.Hkv;
     h = bh - b_kv * p.Hkv;
@@ -197,27 +225,27 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       L = cap;
     }
     if (L < 0) L = 0;
-    row0 = mt * 128;
+    row0 = mt * kTileRows;
     rows_total = p.GQ;
-    const int rows_tile = min(128, p.GQ - row0);
-    const int lim_tile = L - p.q_len + (row0 + rows_tile - 1) / p.G;
+    const int rows_cta = min(kTileRows, p.GQ - row0);
+    const int lim_cta = L - p.q_len + (row0 + rows_cta - 1) / p.G;
     kv_lo = 0;
     kv_end = L;
-    n_chunks = lim_tile < 0 ? 0 : (lim_tile + kChunk) / kChunk;
+    n_chunks = lim_cta < 0 ? 0 : (lim_cta + kChunk) / kChunk;
   }
+  const int ntiles = (row0 + 128 < rows_total) ? 2 : 1;  // MMA tiles holding rows
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_addr(&kv_full[s]), 1);
       mbar_init(smem_addr(&kv_empty[s]), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(smem_addr(&s_full[i]), 1);
-      mbar_init(smem_addr(&s_free[i]), 4);
       mbar_init(smem_addr(&p_full[i]), 4);
       mbar_init(smem_addr(&pv_done[i]), 1);
     }
-    mbar_init(smem_addr(q_ready), 4);
+    mbar_init(smem_addr(q_ready), 8);
     prefetch_tensormap(&tmk);
     prefetch_tensormap(&tmv);
   }
@@ -232,14 +260,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s0 = tmem;        // columns 0..63 / 64..127: S buffers
-  const uint32_t tmem_o = tmem + 128;   // columns 128 .. 128 + D - 1: O
   pdl_wait_previous();
   // The cascade's decode kernel may start its prologue now; it waits for this
   // grid to finish before reading the prefix states.
   if constexpr (kPrefix) pdl_launch_dependents();
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- producer: K/V chunks by TMA ----------------
     int win_base = -1, win_val = -1;
     const int bs = p.bs;
@@ -316,65 +342,76 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
       __syncwarp();
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issue (one thread) ----------------
     if (lane == 0 && n_chunks > 0) {
       bool ok = mbar_wait_bounded(smem_addr(q_ready), 0);
       const uint32_t id_s = umma_idesc(128, kChunk, FMT, 0);
       const uint32_t id_o = umma_idesc(128, D, FMT, 1);
-      const uint32_t q_base = smem_addr(s_q);
-      auto issue_pv = [&](int jp) {
-        const int pb = jp & 1;
-        const uint32_t v_base = smem_addr(s_kv + (jp % S) * KV_BYTES) + HALVES * HALF_BYTES;
-        const uint32_t p_hi = smem_addr(s_p + (2 * pb) * P_BYTES);
-        const uint32_t p_lo = smem_addr(s_p + (2 * pb + 1) * P_BYTES);
-        tmem_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < kChunk / 16; ++ks) {
-          const uint64_t vd = umma_desc(v_base + ks * 2048u, HALF_BYTES, 1024);
-          umma_f16(tmem_o, umma_desc(p_hi + ks * 32u, 16, 1024), vd, id_o, (jp > 0 || ks > 0) ? 1u : 0u);
-          if (kSplit) umma_f16(tmem_o, umma_desc(p_lo + ks * 32u, 16, 1024), vd, id_o, 1u);
-        }
-        umma_commit(smem_addr(&pv_done[pb]));
-        umma_commit(smem_addr(&kv_empty[jp % S]));
-      };
-      auto issue_qk = [&](int jq) -> bool {
-        const int stage = jq % S;
-        const int sb = jq & 1;
-        if (!mbar_wait_bounded(smem_addr(&kv_full[stage]), (uint32_t)((jq / S) & 1))) return false;
-        if (jq >= 2 && !mbar_wait_bounded(smem_addr(&s_free[sb]), (uint32_t)(((jq >> 1) - 1) & 1))) return false;
-        tmem_fence_after();
-        const uint32_t k_base = smem_addr(s_kv + stage * KV_BYTES);
+      auto issue_qk = [&](int t, int jq) {
+        const uint32_t q_base = smem_addr(s_q + t * QT_BYTES);
+        const uint32_t k_base = smem_addr(s_kv + (jq % S) * KV_BYTES);
+        const uint32_t d = tmem + (uint32_t)(t * 256 + (jq & 1) * kChunk);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t hoff = (uint32_t)(ks >> 2);
           const uint32_t koff = (uint32_t)(ks & 3) * 32u;
-          umma_f16(tmem_s0 + sb * kChunk, umma_desc(q_base + hoff * 16384u + koff, 16, 1024),
+          umma_f16(d, umma_desc(q_base + hoff * 16384u + koff, 16, 1024),
                    umma_desc(k_base + hoff * HALF_BYTES + koff, 16, 1024), id_s, ks > 0 ? 1u : 0u);
         }
-        umma_commit(smem_addr(&s_full[sb]));
-        return true;
+        umma_commit(smem_addr(&s_full[t * 2 + (jq & 1)]));
       };
-      // QK^T runs one chunk ahead of PV, so the softmax of chunk j+1 can start
-      // as soon as that of chunk j ends.
-      if (ok) ok = issue_qk(0);
+      auto issue_pv = [&](int t, int jp) {
+        const uint32_t v_base = smem_addr(s_kv + (jp % S) * KV_BYTES) + HALVES * HALF_BYTES;
+        const uint32_t pcol = tmem + (uint32_t)(t * 256 + (jp & 1) * kChunk);  // P hi: +0..31, lo: +32..63
+        const uint32_t o = tmem + (uint32_t)(t * 256 + 128);
+#pragma unroll
+        for (int ks = 0; ks < kChunk / 16; ++ks) {
+          const uint64_t vd = umma_desc(v_base + ks * 2048u, HALF_BYTES, 1024);
+          umma_f16_tmem_a(o, pcol + ks * 8u, vd, id_o, (jp > 0 || ks > 0) ? 1u : 0u);
+          if (kSplit) umma_f16_tmem_a(o, pcol + 32u + ks * 8u, vd, id_o, 1u);
+        }
+        umma_commit(smem_addr(&pv_done[t * 2 + (jp & 1)]));
+      };
+      // S of chunk j+1 (both tiles) is issued before P.V of chunk j, so a
+      // tile's softmax of j+1 overlaps the products of chunk j.
+      if (ok) ok = mbar_wait_bounded(smem_addr(&kv_full[0]), 0);
+      if (ok) {
+        tmem_fence_after();
+        for (int t = 0; t < ntiles; ++t) issue_qk(t, 0);
+      }
       for (int j = 0; j < n_chunks && ok; ++j) {
-        if (j + 1 < n_chunks) {
-          ok = issue_qk(j + 1);
+        const int jn = j + 1;
+        if (jn < n_chunks) {
+          ok = mbar_wait_bounded(smem_addr(&kv_full[jn % S]), (uint32_t)((jn / S) & 1));
+          for (int t = 0; t < ntiles && ok; ++t) {
+            // the buffer's previous P (chunk jn - 2) must have been consumed
+            if (jn >= 2) ok = mbar_wait_bounded(smem_addr(&pv_done[t * 2 + (jn & 1)]), (uint32_t)(((jn - 2) >> 1) & 1));
+            if (ok) {
+              tmem_fence_after();
+              issue_qk(t, jn);
+            }
+          }
           if (!ok) break;
         }
-        ok = mbar_wait_bounded(smem_addr(&p_full[j & 1]), (uint32_t)((j >> 1) & 1));
+        for (int t = 0; t < ntiles && ok; ++t) {
+          ok = mbar_wait_bounded(smem_addr(&p_full[t * 2 + (j & 1)]), (uint32_t)((j >> 1) & 1));
+          if (ok) {
+            tmem_fence_after();
+            issue_pv(t, j);
+          }
+        }
         if (!ok) break;
-        issue_pv(j);
+        umma_commit(smem_addr(&kv_empty[j % S]));
       }
       if (!ok) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
     } else if constexpr (kPrefix) {
       // Idle lanes: every member must reach the shared prefix through the same
       // physical blocks as the first member (whose table the producer reads).
-      // Checked once per member, by the split-0 / head-0 tile holding its first row.
+      // Checked once per member, by the split-0 / head-0 CTA holding its first row.
       if (lane > 0 && split == 0 && h == 0 && prefix_tokens > 0) {
         const int i_lo = (row0 + p.GQ - 1) / p.GQ;
-        const int i_hi = min(rows_total, row0 + 128);  // rows; members i with i*GQ < i_hi
+        const int i_hi = min(rows_total, row0 + kTileRows);  // rows; members i with i*GQ < i_hi
         const int nblk = (prefix_tokens + p.bs - 1) / p.bs;
         bool bad = false;
         for (int i = i_lo; i * p.GQ < i_hi; ++i) {
@@ -393,11 +430,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- softmax warps: thread = query row = TMEM lane ----------------
-    const int r = tid;  // 0..127
-    const int qr = row0 + r;
-    const bool row_ok = qr < rows_total;
-    int t = 0, g = 0, b = b_kv;
+    // ---------------- softmax warps: tile t, thread = query row = TMEM lane ----------------
+    const int t = warp >> 2;             // MMA tile of this warpgroup
+    const int r = (warp & 3) * 32 + lane;  // row within the tile = TMEM lane
+    const bool tile_on = t < ntiles;
+    const int qr = row0 + t * 128 + r;
+    const bool row_ok = tile_on && qr < rows_total;
+    int tq = 0, g = 0, b = b_kv;
     int lim = -1;  // last attendable position of this row
     if (row_ok) {
       int r_in = qr;
@@ -407,34 +446,37 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         b = p.member_seq[moff + i];
         if (b < 0 || b >= p.B) b = b_kv;  // flagged by the table check
       }
-      t = r_in / p.G;
-      g = r_in - t * p.G;
+      tq = r_in / p.G;
+      g = r_in - tq * p.G;
       const int Lb = min(max(p.context_lens[b] + p.len_offset, 0), cap);
-      lim = Lb - p.q_len + t;
+      lim = Lb - p.q_len + tq;
       if constexpr (kPrefix) lim = min(lim, kv_end - 1);
     }
-    // Q row -> swizzled K-major tile (row r)
+    // Q row -> swizzled K-major tile t (row r)
     {
       const T* qrow = static_cast<const T*>(p.q) + (long long)b * p.q_sb + (long long)(h * p.G + g) * p.q_sh +
-                      (long long)t * p.q_st;
+                      (long long)tq * p.q_st;
+      uint8_t* qt = s_q + t * QT_BYTES;
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (row_ok) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        *reinterpret_cast<uint4*>(s_q + (c >> 3) * 16384 + sw128_chunk(r, c & 7)) = v;
+        *reinterpret_cast<uint4*>(qt + (c >> 3) * 16384 + sw128_chunk(r, c & 7)) = v;
       }
     }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_addr(q_ready));
 
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + (uint32_t)(t * 256) + lane_base;  // S / P buffers of this tile
+    const uint32_t t_o = t_s + 128u;                               // O of this tile
     float m_ref = -INFINITY;  // reference max (log2 domain) of this row
     float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_chunks; ++j) {
+    for (int j = 0; j < n_chunks && tile_on; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait_bounded(smem_addr(&s_full[sb]), (uint32_t)((j >> 1) & 1))) {
+      if (!mbar_wait_bounded(smem_addr(&s_full[t * 2 + sb]), (uint32_t)((j >> 1) & 1))) {
         ok = false;
         break;
       }
@@ -442,8 +484,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       float x[kChunk];  // raw scores q.k of this row's 64 tokens
       {
         uint32_t r0[32], r1[32];
-        tmem_ld32(tmem_s0 + sb * kChunk + lane_base, r0);
-        tmem_ld32(tmem_s0 + sb * kChunk + 32 + lane_base, r1);
+        tmem_ld32(t_s + sb * kChunk, r0);
+        tmem_ld32(t_s + sb * kChunk + 32, r1);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -451,10 +493,6 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           x[32 + i] = __uint_as_float(r1[i]);
         }
       }
-      tmem_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&s_free[sb]));
-
       const int tok0 = kv_lo + j * kChunk;
       if (tok0 + kChunk - 1 > lim) {  // causal / end-of-range mask in this chunk
 #pragma unroll
@@ -475,26 +513,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         move = true;
       }
       const float nbase = (m_ref == -INFINITY) ? 0.f : -m_ref;
-      float ps = 0.f;
-      uint32_t phi[kChunk / 2], plo[kChunk / 2];
-#pragma unroll
-      for (int i = 0; i < kChunk; i += 2) {
-        const float p0 = ex2(fmaf(x[i], sl2, nbase));
-        const float p1 = ex2(fmaf(x[i + 1], sl2, nbase));
-        ps += p0 + p1;
-        phi[i / 2] = pack2<T>(p0, p1);
-        if (kSplit) plo[i / 2] = pack2<T>(p0 - lo_half<T>(phi[i / 2]), p1 - hi_half<T>(phi[i / 2]));
-      }
-      l = l * alpha + ps;
 
-      // P buffer sb is free once the PV of chunk j-2 completed
-      if (j >= 2 && !mbar_wait_bounded(smem_addr(&pv_done[sb]), (uint32_t)(((j - 2) >> 1) & 1))) {
-        ok = false;
-        break;
-      }
-      // O rescale (warp-collective TMEM load/store) after the PV of chunk j-1
+      // O rescale (warp-collective TMEM load/store) once the PV of chunk j-1 is done
       if (__any_sync(0xffffffffu, move && j > 0)) {
-        if (!mbar_wait_bounded(smem_addr(&pv_done[(j - 1) & 1]), (uint32_t)(((j - 1) >> 1) & 1))) {
+        if (!mbar_wait_bounded(smem_addr(&pv_done[t * 2 + ((j - 1) & 1)]), (uint32_t)(((j - 1) >> 1) & 1))) {
           ok = false;
           break;
         }
@@ -503,63 +525,72 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
           uint32_t o[32];
-          tmem_ld32(tmem_o + c0 + lane_base, o);
+          tmem_ld32(t_o + c0, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
-          tmem_st32(tmem_o + c0 + lane_base, o);
+          tmem_st32(t_o + c0, o);
         }
-        tmem_wait_st();
       }
-      // P row (K-major, swizzled): 64 tokens x 2 B = 8 chunks of 16 B
-      uint8_t* phi_buf = s_p + (2 * sb) * P_BYTES;
-      uint8_t* plo_buf = s_p + (2 * sb + 1) * P_BYTES;
+      // P row over this chunk's S columns: hi at +0..31, lo at +32..63
+      float ps = 0.f;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        *reinterpret_cast<uint4*>(phi_buf + sw128_chunk(r, c)) =
-            make_uint4(phi[4 * c], phi[4 * c + 1], phi[4 * c + 2], phi[4 * c + 3]);
-        if (kSplit)
-          *reinterpret_cast<uint4*>(plo_buf + sw128_chunk(r, c)) =
-              make_uint4(plo[4 * c], plo[4 * c + 1], plo[4 * c + 2], plo[4 * c + 3]);
+      for (int piece = 0; piece < 4; ++piece) {
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float p0 = ex2(fmaf(x[16 * piece + 2 * i], sl2, nbase));
+          const float p1 = ex2(fmaf(x[16 * piece + 2 * i + 1], sl2, nbase));
+          ps += p0 + p1;
+          hi[i] = pack2<T>(p0, p1);
+          lo[i] = kSplit ? pack2<T>(p0 - lo_half<T>(hi[i]), p1 - hi_half<T>(hi[i])) : 0u;
+        }
+        tmem_st8(t_s + sb * kChunk + piece * 8, hi);
+        if (kSplit) tmem_st8(t_s + sb * kChunk + 32 + piece * 8, lo);
       }
-      // tail chunk: V rows at or past kv_end hold stale data; zero them (P is 0 there)
+      l = l * alpha + ps;
+      // tail chunk: V rows at or past kv_end hold stale data; zero them (P is 0
+      // there).  Tile 0's warpgroup does it before its P is published; the PV of
+      // tile 1 is issued after tile 0's, so it sees the zeros too.
       const int valid = kv_end - tok0;
-      if (valid < kChunk) {
+      if (t == 0 && valid < kChunk) {
         uint8_t* vbase = s_kv + (j % S) * KV_BYTES + HALVES * HALF_BYTES;
         const int nrows = kChunk - valid;
-        for (int i = tid; i < nrows * HALVES * 8; i += 128) {
+        for (int i = r; i < nrows * HALVES * 8; i += 128) {
           const int row = valid + i / (HALVES * 8);
           const int rem = i % (HALVES * 8);
           *reinterpret_cast<uint4*>(vbase + (rem >> 3) * HALF_BYTES + row * 128 + (rem & 7) * 16) =
               make_uint4(0u, 0u, 0u, 0u);
         }
+        fence_proxy_async_smem();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tmem_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&p_full[sb]));
+      if (lane == 0) mbar_arrive(smem_addr(&p_full[t * 2 + sb]));
     }
 
-    // ---- epilogue: O / l -> global ----
-    if (ok && n_chunks > 0) {
+    // ---- epilogue ----
+    if (tile_on && ok && n_chunks > 0) {
       const int jl = n_chunks - 1;
-      ok = mbar_wait_bounded(smem_addr(&pv_done[jl & 1]), (uint32_t)((jl >> 1) & 1));
+      ok = mbar_wait_bounded(smem_addr(&pv_done[t * 2 + (jl & 1)]), (uint32_t)((jl >> 1) & 1));
     }
     if (!ok && lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
     tmem_fence_after();
+    const bool have_o = tile_on && n_chunks > 0;  // warp-uniform
     if constexpr (kPrefix) {
       // (m, l) and the unnormalised O of this row's prefix part, for the decode
       // kernel to fold in; an empty or failed part is (-inf, 0, 0).
       const bool have = ok && l > 0.f;
       const long long ridx = (long long)split * p.B * p.Hq * p.q_len +
-                             ((long long)b * p.Hq + h * p.G + g) * p.q_len + t;
+                             ((long long)b * p.Hq + h * p.G + g) * p.q_len + tq;
       if (row_ok) p.pre_ml[ridx] = make_float2(have ? m_ref : -INFINITY, have ? l : 0.f);
       float* arow = p.pre_acc + ridx * D;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 32) {
         uint32_t o[32];
-        if (n_chunks > 0) {
-          tmem_ld32(tmem_o + c0 + lane_base, o);
+        if (have_o) {
+          tmem_ld32(t_o + c0, o);
           tmem_wait_ld();
         }
         if (row_ok) {
@@ -574,77 +605,74 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         }
       }
       if (p.splits > 1) {
-        // The last split of this tile to finish merges every split's state of
-        // its rows into split 0 (log-sum-exp), so the decode kernel folds one
-        // state per row.
-        __shared__ int s_last;
+        // The last split of this CTA's rows to finish merges every split's
+        // state of those rows into split 0 (log-sum-exp), so the decode kernel
+        // folds one state per row.
         __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps
         if (tid == 0) s_last = atomicAdd(&p.pre_cnt[tile_id], 1) == p.splits - 1;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (s_last) {
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (s_last && row_ok) {
           __threadfence();
           const long long R = (long long)p.B * p.Hq * p.q_len;
           const long long r0 = ridx - (long long)split * R;  // this row in split 0
-          if (row_ok) {
-            float M = -INFINITY;
-            for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(&p.pre_ml[sp * R + r0]).x);
-            const float base = (M == -INFINITY) ? 0.f : M;
-            float lsum = 0.f;
-            for (int sp = 0; sp < p.splits; ++sp) {
-              const float2 ml = __ldcg(&p.pre_ml[sp * R + r0]);
-              lsum += ex2(ml.x - base) * ml.y;
-            }
-            for (int c0 = 0; c0 < D; c0 += 32) {
-              float4 a[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-              for (int sp = 0; sp < p.splits; ++sp) {
-                const float w = ex2(__ldcg(&p.pre_ml[sp * R + r0]).x - base);
-                const float4* src = reinterpret_cast<const float4*>(p.pre_acc + (sp * R + r0) * D + c0);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  const float4 v = __ldcg(src + i);
-                  a[i].x = fmaf(w, v.x, a[i].x);
-                  a[i].y = fmaf(w, v.y, a[i].y);
-                  a[i].z = fmaf(w, v.z, a[i].z);
-                  a[i].w = fmaf(w, v.w, a[i].w);
-                }
-              }
-              float4* dst = reinterpret_cast<float4*>(p.pre_acc + r0 * D + c0);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) dst[i] = a[i];
-            }
-            p.pre_ml[r0] = make_float2(M, lsum);
+          float M = -INFINITY;
+          for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(&p.pre_ml[sp * R + r0]).x);
+          const float base = (M == -INFINITY) ? 0.f : M;
+          float lsum = 0.f;
+          for (int sp = 0; sp < p.splits; ++sp) {
+            const float2 ml = __ldcg(&p.pre_ml[sp * R + r0]);
+            lsum += ex2(ml.x - base) * ml.y;
           }
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            float4 a[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sp = 0; sp < p.splits; ++sp) {
+              const float w = ex2(__ldcg(&p.pre_ml[sp * R + r0]).x - base);
+              const float4* src = reinterpret_cast<const float4*>(p.pre_acc + (sp * R + r0) * D + c0);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 v = __ldcg(src + i);
+                a[i].x = fmaf(w, v.x, a[i].x);
+                a[i].y = fmaf(w, v.y, a[i].y);
+                a[i].z = fmaf(w, v.z, a[i].z);
+                a[i].w = fmaf(w, v.w, a[i].w);
+              }
+            }
+            float4* dst = reinterpret_cast<float4*>(p.pre_acc + r0 * D + c0);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = a[i];
+          }
+          p.pre_ml[r0] = make_float2(M, lsum);
         }
       }
     } else {
-    T* orow = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
-              (long long)t * p.o_st;
-    const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
+      T* orow = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
+                (long long)tq * p.o_st;
+      const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
 #pragma unroll
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      uint32_t o[32];
-      if (n_chunks > 0) {
-        tmem_ld32(tmem_o + c0 + lane_base, o);
-        tmem_wait_ld();
-      } else {
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        if (have_o) {
+          tmem_ld32(t_o + c0, o);
+          tmem_wait_ld();
+        } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0u;
-      }
-      if (row_ok) {
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          uint4 v;
-          v.x = pack2<T>(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
-          v.y = pack2<T>(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-          v.z = pack2<T>(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
-          v.w = pack2<T>(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + c0 + i) = v;
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack2<T>(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
+            v.y = pack2<T>(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+            v.z = pack2<T>(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+            v.w = pack2<T>(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c0 + i) = v;
+          }
         }
       }
-    }
     }
   }
 
@@ -658,7 +686,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 
 size_t prefill_umma_smem_bytes(int D) {
   const size_t halves = (size_t)D / 64;
-  return 1024 + (size_t)kUmmaStages * 2 * halves * kChunk * 128 + halves * 128 * 128 + 4 * 128 * 128 + 256;
+  const size_t stages = D == 128 ? kUmmaStages<128>::value : kUmmaStages<64>::value;
+  return 1024 + stages * 2 * halves * kChunk * 128 + 2 * halves * 128 * 128 + 256;
 }
 
 template <typename T, int D, bool kPrefix>
@@ -674,11 +703,11 @@ static cudaError_t launch_umma_impl(const DecodeParams& p, const CUtensorMap& tm
     if (e != cudaSuccess) return e;
     prepared[dev] = true;
   }
-  const long long tiles =
-      kPrefix ? (long long)p.splits * p.num_groups * p.Hkv * ((p.max_members * p.GQ + 127) / 128)
-              : (long long)p.B * p.Hkv * ((p.GQ + 127) / 128);
+  const long long ctas =
+      kPrefix ? (long long)p.splits * p.num_groups * p.Hkv * (((long long)p.max_members * p.GQ + kTileRows - 1) / kTileRows)
+              : (long long)p.B * p.Hkv * ((p.GQ + kTileRows - 1) / kTileRows);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)tiles);
+  cfg.gridDim = dim3((unsigned)ctas);
   cfg.blockDim = dim3(kUmmaThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

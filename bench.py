@@ -213,6 +213,8 @@ def main() -> None:
                     help="time replays of a CUDA graph holding the step (append + decode) instead of eager calls")
     ap.add_argument("--prefix-sharing", choices=["auto", "on", "off"], default="auto",
                     help="cascade over shared prompt prefixes (auto: when the workload has them)")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="KV-head sharding: all-gather inside the decode kernel over NVLink, or NCCL after it")
     ap.add_argument("--shard", choices=["auto", "seq", "head"], default="auto",
                     help="multi-GPU layout: sequences (weak scaling) or KV heads + NCCL all-gather "
                          "(strong scaling); auto = heads for cfg5-llama3-70b, sequences otherwise")
@@ -227,7 +229,8 @@ def main() -> None:
     import torch.distributed as dist
 
     from llm_serving_runtime_b200 import _lib, paged_attention_decode
-    from llm_serving_runtime_b200.sharding import HeadShardedDecode, kv_head_range, shard_sequences
+    from llm_serving_runtime_b200.sharding import FusedHeadGather, HeadShardedDecode, kv_head_range, \
+        shard_sequences
     from llm_serving_runtime_b200.workloads import SPECS, algorithmic_bytes, attention_flops, make_workload, \
         sample_lengths
 
@@ -249,7 +252,7 @@ def main() -> None:
         # every rank holds its KV heads of the whole batch; outputs all-gathered
         GB = spec.batch
         w = make_workload(spec, device=dev, kv_heads=kv_head_range(spec.num_kv_heads, world, rank))
-        gather = HeadShardedDecode()
+        gather = FusedHeadGather() if args.gather == "fused" else HeadShardedDecode()
     else:
         GB = spec.batch * world
         lens = sample_lengths(spec, GB) + spec.q_len
@@ -284,6 +287,9 @@ def main() -> None:
     def step():
         if graph is not None:
             return graph.replay()[0]
+        if isinstance(gather, FusedHeadGather):  # returns this rank's gathered output
+            return gather(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                          w.slot_mapping, w.new_key, w.new_value)
         if gather is not None:
             return gather(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
                           w.slot_mapping, w.new_key, w.new_value, out=out)
@@ -367,8 +373,10 @@ def main() -> None:
 
     host_in = [{k: _src(k).cpu().pin_memory() for k in names + pg_names} for _ in range(2)]
     dev_in = [{k: torch.empty_like(_src(k)) for k in names + pg_names} for _ in range(2)]
-    dev_out = [torch.empty_like(out) for _ in range(2)]
     full_out_shape = (B, spec.num_q_heads, q, spec.head_dim) if shard == "head" else tuple(out.shape)
+    fused = isinstance(gather, FusedHeadGather)
+    dev_out = [torch.empty(full_out_shape, dtype=out.dtype, device=dev) if fused else torch.empty_like(out)
+               for _ in range(2)]
     host_out = [torch.empty(full_out_shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in host_in[0].values())
     d2h = host_out[0].numel() * host_out[0].element_size()
@@ -461,7 +469,8 @@ def main() -> None:
             "workload": args.workload, "global_batch": GB, "q_len": q, "num_q_heads": spec.num_q_heads,
             "num_kv_heads": spec.num_kv_heads, "head_dim": spec.head_dim, "block_size": spec.block_size,
             "context_lens": f"{spec.length_dist} [{spec.length_lo}, {spec.length_hi}]",
-            "parallelism": (f"kvhead-shard{world}+allgather" if shard == "head" else f"seq-shard{world}")
+            "parallelism": ((f"kvhead-shard{world}+fused-gather" if args.gather == "fused"
+                             else f"kvhead-shard{world}+allgather") if shard == "head" else f"seq-shard{world}")
             if world > 1 else "single",
             "l2": "inputs larger than L2 (no flush)",
             "launch": "cuda-graph replay" if args.graph else "eager",

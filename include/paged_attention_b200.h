@@ -190,6 +190,46 @@ PA_API size_t pa_cascade_workspace_bytes(int32_t batch, int32_t num_q_heads, int
                                          int32_t q_len, int32_t head_dim, int32_t dtype, int32_t device,
                                          int32_t num_groups, int32_t max_members, int32_t max_prefix_len);
 
+/* ---- KV-head-sharded decode with the all-gather fused in (one process per GPU) ----
+ * Each rank attends its own KV heads of every sequence; the decode kernel writes
+ * every finished output row straight into EVERY rank's gathered output
+ * [batch, total query heads, q_len, head_dim] (peer memory over NVLink), then
+ * the grid's last warp raises this rank's flag at every rank and waits, for at
+ * most wait_ns, until every rank has raised its own.  Replaces the local decode
+ * + all-gather (an NCCL collective plus a copy) of the sharded layout; the
+ * reference runs on one GPU and has no counterpart.
+ * Buffers of other ranks are reached through CUDA IPC: pa_ipc_export on the
+ * owner, pa_ipc_import in every other process. */
+#define PA_IPC_HANDLE_BYTES 64
+typedef struct pa_ipc_handle {
+  unsigned char bytes[PA_IPC_HANDLE_BYTES]; /* cudaIpcMemHandle_t of the allocation */
+  int64_t offset;                           /* of the exported pointer within it */
+} pa_ipc_handle;
+
+/* Handle for `device_ptr` (any pointer into a cudaMalloc'd allocation). */
+PA_API int pa_ipc_export(const void* device_ptr, pa_ipc_handle* handle);
+/* Map another process's exported pointer into this one (*device_ptr receives it). */
+PA_API int pa_ipc_import(const pa_ipc_handle* handle, void** device_ptr);
+/* Unmap a pointer pa_ipc_import returned. */
+PA_API int pa_ipc_release(void* device_ptr);
+
+typedef struct pa_gather_args {
+  int32_t num_ranks, rank;
+  int32_t head_offset;           /* first query head of this rank in the gathered output */
+  void* const* out_ranks;        /* device array [num_ranks]: every rank's gathered output
+                                    (this process's mapping); args->out must be out_ranks[rank] */
+  uint32_t* const* flags_ranks;  /* device array [num_ranks]: every rank's flag words [num_ranks] */
+  uint32_t* epoch;               /* this rank's call counter (device, starts at 0 like the flags) */
+  uint32_t* done_warps;          /* this rank's warp counter (device, zero between calls) */
+  int64_t wait_ns;               /* bound on the wait for the other ranks' flags */
+} pa_gather_args;
+
+/* pa_decode for the local KV heads, output rows written to every rank's gathered
+ * output at query-head offset head_offset (args->out_stride_* are the gathered
+ * output's strides).  fp16/bf16 only.  A rank whose flag does not arrive in time
+ * is reported as PA_DEVERR_WAIT_TIMEOUT; no wait is unbounded. */
+PA_API int pa_decode_gather(const pa_decode_args* args, const pa_gather_args* gather, void* stream);
+
 /* Size of the scratch array behind pa_decode_static_workspace (16 MiB). */
 #define PA_STATIC_WORKSPACE_BYTES (16u << 20)
 

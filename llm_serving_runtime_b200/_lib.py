@@ -37,6 +37,10 @@ EXPORTED_SYMBOLS = (
     "pa_decode_static_workspace",
     "pa_decode_cascade",
     "pa_cascade_workspace_bytes",
+    "pa_decode_gather",
+    "pa_ipc_export",
+    "pa_ipc_import",
+    "pa_ipc_release",
     "pa_decode_workspace_bytes",
     "pa_workspace_init",
     "pa_read_device_errors",
@@ -115,6 +119,26 @@ class PrefixGroupsArgs(ctypes.Structure):
     ]
 
 
+PA_IPC_HANDLE_BYTES = 64
+
+
+class IpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * PA_IPC_HANDLE_BYTES), ("offset", _i64)]
+
+
+class GatherArgs(ctypes.Structure):
+    _fields_ = [
+        ("num_ranks", _i32),
+        ("rank", _i32),
+        ("head_offset", _i32),
+        ("out_ranks", _vp),
+        ("flags_ranks", _vp),
+        ("epoch", _vp),
+        ("done_warps", _vp),
+        ("wait_ns", _i64),
+    ]
+
+
 _lock = threading.Lock()
 _handle: ctypes.CDLL | None = None
 
@@ -141,6 +165,14 @@ def load() -> ctypes.CDLL:
         lib.pa_decode_cascade.argtypes = [ctypes.POINTER(DecodeArgs), ctypes.POINTER(PrefixGroupsArgs), _vp]
         lib.pa_cascade_workspace_bytes.restype = _sz
         lib.pa_cascade_workspace_bytes.argtypes = [_i32] * 10
+        lib.pa_decode_gather.restype = ctypes.c_int
+        lib.pa_decode_gather.argtypes = [ctypes.POINTER(DecodeArgs), ctypes.POINTER(GatherArgs), _vp]
+        lib.pa_ipc_export.restype = ctypes.c_int
+        lib.pa_ipc_export.argtypes = [_vp, ctypes.POINTER(IpcHandle)]
+        lib.pa_ipc_import.restype = ctypes.c_int
+        lib.pa_ipc_import.argtypes = [ctypes.POINTER(IpcHandle), ctypes.POINTER(_vp)]
+        lib.pa_ipc_release.restype = ctypes.c_int
+        lib.pa_ipc_release.argtypes = [_vp]
         lib.pa_decode_workspace_bytes.restype = _sz
         lib.pa_decode_workspace_bytes.argtypes = [_i32, _i32, _i32, _i32, _i32, _i32, _i32]
         lib.pa_workspace_init.restype = ctypes.c_int

@@ -76,6 +76,36 @@ int get_encode(PFN_cuTensorMapEncodeTiled_v12000* fn) {
   return PA_OK;
 }
 
+// cuMemGetAddressRange (driver API), fetched like the tensor-map encoder: the
+// allocation a pointer lies in, which is what CUDA IPC exports.
+PFN_cuMemGetAddressRange_v3020 g_addr_range = nullptr;
+
+int get_addr_range(PFN_cuMemGetAddressRange_v3020* fn) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_addr_range == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || ptr == nullptr)
+      return fail(PA_ERR_CUDA, "cuMemGetAddressRange entry point unavailable");
+    g_addr_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(ptr);
+  }
+  *fn = g_addr_range;
+  return PA_OK;
+}
+
+int allocation_base(const void* ptr, char** base) {
+  PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  int st = get_addr_range(&fn);
+  if (st != PA_OK) return st;
+  CUdeviceptr b = 0;
+  size_t size = 0;
+  CUresult r = fn(&b, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(PA_ERR_INVALID_ARGUMENT, "pointer is not device memory (CUresult %d)", (int)r);
+  *base = reinterpret_cast<char*>(b);
+  return PA_OK;
+}
+
 int elem_bytes(int dtype) { return dtype == PA_DTYPE_FLOAT32 ? 4 : 2; }
 
 bool aligned_ptr(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -313,9 +343,61 @@ size_t pa_cascade_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t nu
   return base + c.ml_bytes + c.acc_bytes + c.cnt_bytes;
 }
 
-static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, void* stream);
+static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, const pa_gather_args* gat,
+                       void* stream);
 
-int pa_decode(const pa_decode_args* a, void* stream) { return decode_impl(a, nullptr, stream); }
+int pa_decode(const pa_decode_args* a, void* stream) { return decode_impl(a, nullptr, nullptr, stream); }
+
+int pa_ipc_export(const void* device_ptr, pa_ipc_handle* handle) {
+  g_last_error[0] = 0;
+  if (device_ptr == nullptr || handle == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null pointer");
+  char* base = nullptr;
+  int st = allocation_base(device_ptr, &base);
+  if (st != PA_OK) return st;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == PA_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle->bytes, &h, sizeof(h));
+  handle->offset = static_cast<const char*>(device_ptr) - base;
+  return PA_OK;
+}
+
+int pa_ipc_import(const pa_ipc_handle* handle, void** device_ptr) {
+  g_last_error[0] = 0;
+  if (handle == nullptr || device_ptr == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle->bytes, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *device_ptr = static_cast<char*>(base) + handle->offset;
+  return PA_OK;
+}
+
+int pa_ipc_release(void* device_ptr) {
+  g_last_error[0] = 0;
+  if (device_ptr == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null pointer");
+  char* base = nullptr;
+  int st = allocation_base(device_ptr, &base);
+  if (st != PA_OK) return st;
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return PA_OK;
+}
+
+int pa_decode_gather(const pa_decode_args* a, const pa_gather_args* g, void* stream) {
+  g_last_error[0] = 0;
+  if (a == nullptr || g == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null args");
+  if (g->num_ranks < 1 || g->rank < 0 || g->rank >= g->num_ranks)
+    return fail(PA_ERR_INVALID_ARGUMENT, "rank %d of %d ranks", g->rank, g->num_ranks);
+  if (g->out_ranks == nullptr || g->flags_ranks == nullptr || g->epoch == nullptr || g->done_warps == nullptr)
+    return fail(PA_ERR_INVALID_ARGUMENT, "gather needs out_ranks, flags_ranks, epoch and done_warps");
+  if (g->head_offset < 0 || g->wait_ns <= 0)
+    return fail(PA_ERR_INVALID_ARGUMENT, "head_offset must be >= 0 and wait_ns > 0");
+  if (a->dtype == PA_DTYPE_FLOAT32) return fail(PA_ERR_UNSUPPORTED, "the fused gather supports fp16/bf16");
+  return decode_impl(a, nullptr, g, stream);
+}
 
 int pa_decode_cascade(const pa_decode_args* a, const pa_prefix_groups* grp, void* stream) {
   g_last_error[0] = 0;
@@ -328,10 +410,11 @@ int pa_decode_cascade(const pa_decode_args* a, const pa_prefix_groups* grp, void
     if (grp->max_members <= 0 || grp->max_prefix_len < 0)
       return fail(PA_ERR_INVALID_ARGUMENT, "max_members must be positive and max_prefix_len non-negative");
   }
-  return decode_impl(a, grp->num_groups > 0 ? grp : nullptr, stream);
+  return decode_impl(a, grp->num_groups > 0 ? grp : nullptr, nullptr, stream);
 }
 
-static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, void* stream) {
+static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, const pa_gather_args* gat,
+                       void* stream) {
   g_last_error[0] = 0;
   if (a == nullptr) return fail(PA_ERR_INVALID_ARGUMENT, "null args");
   const int dtype = a->dtype;
@@ -452,6 +535,16 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, voi
   char* ws = static_cast<char*>(a->workspace);
   p.counters = reinterpret_cast<int32_t*>(ws + pa::kWsHeaderBytes);
   p.partials = reinterpret_cast<float*>(ws + pa::kWsHeaderBytes + pa::ws_counter_bytes(p.nw_total));
+  if (gat != nullptr) {
+    p.out_ranks = gat->out_ranks;
+    p.flags_ranks = gat->flags_ranks;
+    p.epoch = gat->epoch;
+    p.done_warps = gat->done_warps;
+    p.n_ranks = gat->num_ranks;
+    p.rank = gat->rank;
+    p.head_offset = gat->head_offset;
+    p.wait_ns = gat->wait_ns;
+  }
   if (cascade) {
     p.seq_group = grp->seq_group;
     p.group_prefix = grp->prefix_lens;
@@ -496,6 +589,14 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, voi
   // 128-row tiles to fill the GPU: the multi-query kernel shares each K/V tile
   // across 128 rows.  Otherwise the split-K decode kernel.
   const long long prefill_tiles = (long long)p.B * p.Hkv * ((p.GQ + 127) / 128);
+  if (gat != nullptr) {
+    // the split-K decode kernel stores every output row to every rank and ends
+    // with the ranks' flag exchange
+    g_last_kernel = "pa::decode_mma_kernel<gather>";
+    e = pa::launch_decode_mma(p, tmk, tmv, dtype, grid, smem, pdl, strm);
+    if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+    return PA_OK;
+  }
   if (cascade) {
     // Prefix pass (tcgen05), then the decode kernel over each member's own
     // tokens, which folds the prefix states in; it waits for the prefix grid.

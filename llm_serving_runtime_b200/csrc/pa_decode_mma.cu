@@ -56,9 +56,43 @@ __device__ __forceinline__ int group_units(int L, int mg, const DecodeParams& p)
   return lim < 0 ? 0 : (lim + kUnitTokens) / kUnitTokens;
 }
 
-// kCascade: the call carries shared-prefix groups (pa_decode_cascade); each
-// member's prefix units are skipped and the prefix states folded into its rows.
-template <typename T, int D, bool kCascade>
+// The fused all-gather's end of a call, run by the grid's last warp: raise
+// this rank's flag (the call's epoch) at every rank with a system-scope release
+// and wait, at most p.wait_ns, until every rank's flag in this rank's array
+// reached the epoch.  The other ranks' output rows in this rank's gathered
+// output are visible once their flags are (each warp fenced its stores before
+// counting itself done).
+__device__ __noinline__ void gather_barrier(uint32_t* const* flags_ranks, uint32_t* epoch, uint32_t* done_warps,
+                                            int n_ranks, int rank, int64_t wait_ns, uint32_t* status, int lane) {
+  __threadfence();
+  const uint32_t e = *epoch + 1u;
+  __syncwarp();
+  if (lane == 0) {
+    *done_warps = 0u;  // ready for the next call
+    *epoch = e;
+  }
+  __threadfence_system();
+  for (int i = lane; i < n_ranks; i += 32) st_release_sys(flags_ranks[i] + rank, e);
+  const uint32_t* mine = flags_ranks[rank];
+  bool ok = true;
+  for (int i = lane; i < n_ranks; i += 32) {
+    const uint64_t t0 = global_ns();
+    while ((int)(ld_acquire_sys(mine + i) - e) < 0) {
+      if (global_ns() - t0 > (uint64_t)wait_ns) {
+        ok = false;
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  if (!__all_sync(0xffffffffu, ok) && lane == 0) raise_flag(status, PA_DEVERR_WAIT_TIMEOUT);
+}
+
+// kMode 1 (cascade): the call carries shared-prefix groups (pa_decode_cascade);
+// each member's prefix units are skipped and the prefix states folded into its
+// rows.  kMode 2 (gather): output rows go to every rank's gathered output
+// (pa_decode_gather).  kMode 0: plain decode.
+template <typename T, int D, int kMode>
 __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                       const DecodeParams p) {
@@ -81,7 +115,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   // Cascade (shared prefixes): the prefix kernel has attended each member's
   // first s_u0[b] units; the work list starts every sequence after them.
   int* s_u0 = s_pref + p.B + 1;
-  constexpr bool cascade = kCascade;
+  constexpr bool cascade = kMode == 1;
+  constexpr bool gather = kMode == 2;
   __shared__ int s_warp_tot[kDecodeWarps];
 
   const int tid = threadIdx.x;
@@ -146,6 +181,26 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   fence_mbar_init();
   __syncthreads();
 
+  // Output row (b, query head hq, token t) in destination dst: this call's
+  // output, or under the fused gather rank dst's gathered output.
+  const int n_dst = gather ? p.n_ranks : 1;
+  auto out_row = [&](int dst, int b, int hq, int t) -> T* {
+    T* base = gather ? static_cast<T*>(p.out_ranks[dst]) : static_cast<T*>(p.out);
+    return base + (long long)b * p.o_sb + (long long)((gather ? p.head_offset : 0) + hq) * p.o_sh +
+           (long long)t * p.o_st;
+  };
+  // Every warp passes here exactly once, when it has stored all its rows.
+  auto finish_warp = [&]() {
+    if constexpr (gather) {
+      __threadfence_system();  // this warp's row stores, local and remote, before its count
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(p.done_warps, 1u) == gridDim.x * kDecodeWarps - 1u;
+      if (__shfl_sync(0xffffffffu, last, 0))
+        gather_barrier(p.flags_ranks, p.epoch, p.done_warps, p.n_ranks, p.rank, p.wait_ns, p.status, lane);
+    }
+  };
+
   // Units of row group mg of sequence b in the work list.
   auto units_of = [&](int b, int mg) -> int {
     const int n = group_units(s_lens[b], mg, p);
@@ -166,8 +221,6 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           const int h = hr / rows;
           const int qr = 16 * mg + (hr - h * rows);
           const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
-          T* o = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
-                 (long long)t * p.o_st + 2 * d2;
           uint32_t v = 0u;
           if (pre) {  // merged prefix state: out = acc / l
             const long long ridx = ((long long)b * p.Hq + h * p.G + g) * p.q_len + t;
@@ -176,7 +229,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
             const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
             v = pack2<T>(a.x * inv, a.y * inv);
           }
-          *reinterpret_cast<uint32_t*>(o) = v;
+          for (int dst = 0; dst < n_dst; ++dst)
+            *reinterpret_cast<uint32_t*>(out_row(dst, b, h * p.G + g, t) + 2 * d2) = v;
         }
       }
     }
@@ -189,15 +243,20 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   if constexpr (cascade) fill_empty_rows();
 
   const long long W = s_pref[B];
-  if (W == 0) return;
+  if (W == 0) {
+    finish_warp();
+    return;
+  }
   long long nw_eff = (W + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
   if (nw_eff > p.nw_total) nw_eff = p.nw_total;
   if (nw_eff < 1) nw_eff = 1;
   const int gw = blockIdx.x * kDecodeWarps + warp;
-  if (gw >= nw_eff) return;
   const long long ws = W * gw / nw_eff;
   const long long we = W * (gw + 1) / nw_eff;
-  if (ws >= we) return;
+  if (gw >= nw_eff || ws >= we) {
+    finish_warp();
+    return;
+  }
 
   // Locate the first unit of this warp's slice.
   // Flat order: sequence, then kv head, then row group, then unit; a sequence
@@ -382,6 +441,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         mbar_wait_bounded(my_bars + (uint32_t)s * 8u, (phase >> s) & 1u);
         s = (s + 1 == stages) ? 0 : s + 1;
       }
+      finish_warp();
       return;
     }
     phase ^= (1u << slot);
@@ -414,23 +474,16 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       const bool r1_ok = qrow0 + 8 < rows_here;
       if (row_end && piece_from_row_start) {
         // The whole row is in this piece: normalise and store.
-        T* op0 = nullptr;
-        T* op1 = nullptr;
-        if (r0_ok) {
-          const int qr = mg * 16 + qrow0;
-          const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
-          op0 = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
-                (long long)t * p.o_st;
-        }
-        if (r1_ok) {
-          const int qr = mg * 16 + qrow0 + 8;
-          const int t = qr / p.G, g = qr - (qr / p.G) * p.G;
-          op1 = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
-                (long long)t * p.o_st;
-        }
-        if (cascade && s_u0[b] > 0) {
+        const int qa0 = mg * 16 + qrow0, qa1 = qa0 + 8;
+        T* op0 = r0_ok ? out_row(0, b, h * p.G + qa0 % p.G, qa0 / p.G) : nullptr;
+        T* op1 = r1_ok ? out_row(0, b, h * p.G + qa1 % p.G, qa1 / p.G) : nullptr;
+        if constexpr (gather) {
+          for (int dst = 0; dst < n_dst; ++dst)
+            store_rows<T, D>(r0_ok ? out_row(dst, b, h * p.G + qa0 % p.G, qa0 / p.G) : nullptr,
+                             r1_ok ? out_row(dst, b, h * p.G + qa1 % p.G, qa1 / p.G) : nullptr, o_acc, lt0, lt1,
+                             quad);
+        } else if (cascade && s_u0[b] > 0) {
           const long long rb = (long long)b * p.Hq + h * p.G;
-          const int qa0 = mg * 16 + qrow0, qa1 = qa0 + 8;
           const long long ridx0 = (rb + qa0 % p.G) * p.q_len + qa0 / p.G;
           const long long ridx1 = (rb + qa1 % p.G) * p.q_len + qa1 / p.G;
           store_rows_folded<T, D>(op0, op1, o_acc, m0, m1, lt0, lt1, ridx0, ridx1, p, quad);
@@ -562,10 +615,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
                   for (int k = 0; k < DPL; ++k) acc[r][k] = fmaf(acc[r][k], c, w * pa[k]);
                 }
                 const float inv = lsum[r] > 0.f ? 1.f / lsum[r] : 0.f;
-                T* op = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
-                        (long long)t * p.o_st;
+                for (int dst = 0; dst < n_dst; ++dst) {
+                  T* op = out_row(dst, b, h * p.G + g, t);
 #pragma unroll
-                for (int k = 0; k < DPL; ++k) op[lane + 32 * k] = from_float<T>(acc[r][k] * inv);
+                  for (int k = 0; k < DPL; ++k) op[lane + 32 * k] = from_float<T>(acc[r][k] * inv);
+                }
               }
             }
           }
@@ -578,6 +632,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     ++cf;
     slot = (slot + 1 == stages) ? 0 : slot + 1;
   }
+  finish_warp();
 }
 
 size_t decode_mma_smem_bytes(int D, int B, int stages, bool cascade) {
@@ -586,7 +641,7 @@ size_t decode_mma_smem_bytes(int D, int B, int stages, bool cascade) {
          (size_t)((cascade ? 3 : 2) * B + 1) * 4;
 }
 
-template <typename T, int D, bool kCascade>
+template <typename T, int D, int kMode>
 static cudaError_t launch_mma_impl(const DecodeParams& p, const CUtensorMap& tmk,
                                    const CUtensorMap& tmv, int grid, size_t smem, bool pdl,
                                    cudaStream_t stream) {
@@ -600,42 +655,45 @@ static cudaError_t launch_mma_impl(const DecodeParams& p, const CUtensorMap& tmk
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = pdl ? attr : nullptr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<T, D, kCascade>, tmk, tmv, p);
+  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<T, D, kMode>, tmk, tmv, p);
 }
 
-template <bool kCascade>
+template <int kMode>
 static cudaError_t launch_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
                               int grid, size_t smem, bool pdl, cudaStream_t stream) {
   if (dtype == PA_DTYPE_BFLOAT16) {
-    if (p.D == 128) return launch_mma_impl<__nv_bfloat16, 128, kCascade>(p, tmk, tmv, grid, smem, pdl, stream);
-    if (p.D == 64) return launch_mma_impl<__nv_bfloat16, 64, kCascade>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 128) return launch_mma_impl<__nv_bfloat16, 128, kMode>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 64) return launch_mma_impl<__nv_bfloat16, 64, kMode>(p, tmk, tmv, grid, smem, pdl, stream);
   } else if (dtype == PA_DTYPE_FLOAT16) {
-    if (p.D == 128) return launch_mma_impl<__half, 128, kCascade>(p, tmk, tmv, grid, smem, pdl, stream);
-    if (p.D == 64) return launch_mma_impl<__half, 64, kCascade>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 128) return launch_mma_impl<__half, 128, kMode>(p, tmk, tmv, grid, smem, pdl, stream);
+    if (p.D == 64) return launch_mma_impl<__half, 64, kMode>(p, tmk, tmv, grid, smem, pdl, stream);
   }
   return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
                               int dtype, int grid, size_t smem, bool pdl, cudaStream_t stream) {
-  return p.seq_group != nullptr ? launch_mma<true>(p, tmk, tmv, dtype, grid, smem, pdl, stream)
-                                : launch_mma<false>(p, tmk, tmv, dtype, grid, smem, pdl, stream);
+  if (p.out_ranks != nullptr) return launch_mma<2>(p, tmk, tmv, dtype, grid, smem, pdl, stream);
+  if (p.seq_group != nullptr) return launch_mma<1>(p, tmk, tmv, dtype, grid, smem, pdl, stream);
+  return launch_mma<0>(p, tmk, tmv, dtype, grid, smem, pdl, stream);
 }
 
-template <bool kCascade>
+template <int kMode>
 static const void* decode_fn(int dtype, int D) {
   if (dtype == PA_DTYPE_BFLOAT16)
-    return D == 128 ? (const void*)decode_mma_kernel<__nv_bfloat16, 128, kCascade>
-                    : (const void*)decode_mma_kernel<__nv_bfloat16, 64, kCascade>;
-  return D == 128 ? (const void*)decode_mma_kernel<__half, 128, kCascade>
-                  : (const void*)decode_mma_kernel<__half, 64, kCascade>;
+    return D == 128 ? (const void*)decode_mma_kernel<__nv_bfloat16, 128, kMode>
+                    : (const void*)decode_mma_kernel<__nv_bfloat16, 64, kMode>;
+  return D == 128 ? (const void*)decode_mma_kernel<__half, 128, kMode>
+                  : (const void*)decode_mma_kernel<__half, 64, kMode>;
 }
 
 cudaError_t decode_mma_prepare(int dtype, int D, size_t smem) {
-  cudaError_t e = cudaFuncSetAttribute(decode_fn<false>(dtype, D), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(decode_fn<true>(dtype, D), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const void* fns[3] = {decode_fn<0>(dtype, D), decode_fn<1>(dtype, D), decode_fn<2>(dtype, D)};
+  for (const void* fn : fns) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace pa

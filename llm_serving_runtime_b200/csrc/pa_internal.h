@@ -68,6 +68,16 @@ struct DecodeParams {
   float* pre_acc;               // [splits][B * Hq * q_len][D]
   int32_t* pre_cnt;             // [num_groups * Hkv * tiles] split arrival counters (zeroed per call)
   int32_t num_groups, max_members, max_prefix, splits, split_tokens;
+  // Fused all-gather of KV-head-sharded decoding (pa_decode_gather); out_ranks
+  // is null otherwise.  Output row (b, hq, t) goes to every rank's gathered
+  // output at query head head_offset + hq; the grid's last warp then raises
+  // this rank's flag (epoch) at every rank and waits for every rank's flag.
+  void* const* out_ranks;       // [n_ranks] gathered outputs (this process's mappings)
+  uint32_t* const* flags_ranks; // [n_ranks] flag arrays [n_ranks]
+  uint32_t* epoch;              // this rank's call counter
+  uint32_t* done_warps;         // warps finished in this call (zero between calls)
+  int32_t n_ranks, rank, head_offset;
+  int64_t wait_ns;
 };
 
 struct AppendParams {
@@ -100,6 +110,8 @@ size_t ws_partial_bytes(int nw_total, int slot_rows, int D);
 
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_kv_append(const AppendParams& p, cudaStream_t stream);
+// Mode follows the params: cascade when seq_group is set, fused gather when
+// out_ranks is set, plain otherwise.
 cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
                               int dtype, int grid, size_t smem, bool pdl, cudaStream_t stream);
 cudaError_t launch_decode_f32(const DecodeParams& p, bool pdl, cudaStream_t stream);

@@ -309,12 +309,18 @@ def paged_attention_decode(
     workspace: torch.Tensor | None = None,
     validate: bool | None = None,
     prefix_groups=None,
+    gather=None,
 ) -> torch.Tensor:
     """Append this step's K/V (optional) and attend; returns [B, Hq, q_len, D].
 
     ``prefix_groups`` (a ``prefix_sharing.PrefixGroups``) marks rows whose
     tables share leading physical blocks: the call then attends each shared
-    block once per group (cascade) and returns the same result."""
+    block once per group (cascade) and returns the same result.
+
+    ``gather`` (internal: a ``_lib.GatherArgs`` with ``total_heads`` attached,
+    built by ``sharding.FusedHeadGather``) makes ``out`` this rank's gathered
+    output [B, total query heads, q_len, D] and writes the local heads' rows to
+    every rank's gathered output in the same kernel."""
     _check_cache_pair(key_cache, value_cache)
     device = key_cache.device
     if query.dim() != 4:
@@ -342,9 +348,12 @@ def paged_attention_decode(
         raise ValueError("key and value must be given together")
     if slot_mapping is not None and key is None:
         raise ValueError("slot_mapping needs key and value")
+    out_heads = Hq if gather is None else gather.total_heads
     if out is None:
+        if gather is not None:
+            raise ValueError("the fused gather writes into the gathered output given as out")
         out = torch.empty((B, Hq, q_len, D), dtype=query.dtype, device=device)
-    elif tuple(out.shape) != (B, Hq, q_len, D) or out.dtype != query.dtype or out.device != device \
+    elif tuple(out.shape) != (B, out_heads, q_len, D) or out.dtype != query.dtype or out.device != device \
             or out.stride(3) != 1:
         raise ValueError("out must be [batch, num_q_heads, q_len, head_dim] in the query dtype")
     if B == 0:
@@ -392,7 +401,10 @@ def paged_attention_decode(
     args.workspace_bytes = workspace.numel()
     args.allow_overlap_with_previous = 1 if appended else 0
     with _with_device(device):
-        if cascade:
+        if gather is not None:
+            _lib.check(lib.pa_decode_gather(ctypes.byref(args), ctypes.byref(gather), _stream_ptr(device)),
+                       "pa_decode_gather")
+        elif cascade:
             groups = prefix_groups.to_args()
             _lib.check(lib.pa_decode_cascade(ctypes.byref(args), ctypes.byref(groups), _stream_ptr(device)),
                        "pa_decode_cascade")

@@ -10,9 +10,11 @@ Two layouts, matching how the work divides:
 
 * KV-head sharding (large models: few KV heads, long contexts).  Rank r holds
   KV heads [r*Hkv/N, (r+1)*Hkv/N) of every sequence and the query heads that
-  read them; block tables and lengths are replicated.  ``HeadShardedDecode``
-  runs the local decode and all-gathers the per-rank outputs (NCCL over
-  NVLink) into the full [B, Hq, q_len, D] result.
+  read them; block tables and lengths are replicated.  ``FusedHeadGather``
+  has the decode kernel itself write every output row into every rank's
+  gathered [B, Hq, q_len, D] output over NVLink (CUDA IPC peer mappings) and
+  end with a bounded flag exchange between the ranks; ``HeadShardedDecode`` is
+  the unfused form (local decode, then an NCCL all-gather and a reorder).
 """
 
 from __future__ import annotations
@@ -20,12 +22,15 @@ from __future__ import annotations
 from collections.abc import Callable
 from dataclasses import dataclass
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .workloads import lpt_partition
 
-__all__ = ["shard_sequences", "kv_head_range", "HeadShardedDecode"]
+__all__ = ["shard_sequences", "kv_head_range", "HeadShardedDecode", "FusedHeadGather"]
 
 
 def shard_sequences(attended_lengths, world: int, group_size: int = 0) -> list[list[int]]:
@@ -77,3 +82,115 @@ class HeadShardedDecode:
             self._gather_buf = torch.empty(shape, dtype=local.dtype, device=local.device)
         dist.all_gather_into_tensor(self._gather_buf, local.contiguous(), group=self.group)
         return self._gather_buf.view(world, B, hl, q, D).permute(1, 0, 2, 3, 4).reshape(B, world * hl, q, D)
+
+
+# Peer allocations mapped into this process, by IPC handle: an allocation is
+# opened once however many buffers inside it are shared.
+_ipc_bases: dict[bytes, int] = {}
+
+
+def _ipc_import(handle_bytes: bytes, offset: int) -> int:
+    base = _ipc_bases.get(handle_bytes)
+    if base is None:
+        h = _lib.IpcHandle()
+        ctypes.memmove(h.bytes, handle_bytes, _lib.PA_IPC_HANDLE_BYTES)
+        h.offset = 0
+        ptr = ctypes.c_void_p()
+        _lib.check(_lib.load().pa_ipc_import(ctypes.byref(h), ctypes.byref(ptr)), "pa_ipc_import")
+        base = int(ptr.value)
+        _ipc_bases[handle_bytes] = base
+    return base + offset
+
+
+class _GatherState:
+    def __init__(self, key, blob, outs, out_ranks, flags_ranks, counters):
+        self.key, self.blob, self.outs = key, blob, outs
+        self.out_ranks, self.flags_ranks, self.counters = out_ranks, flags_ranks, counters
+
+
+class FusedHeadGather:
+    """KV-head-sharded decode with the all-gather fused into the decode kernel.
+
+    Called like ``HeadShardedDecode`` (the local heads' query and caches, the
+    replicated tables and lengths) and returns [B, Hq, q_len, D] in the global
+    head order.  Every rank must make the same calls in the same order.  The
+    decode kernel stores each finished row of this rank's heads into every
+    rank's gathered output (peer memory over NVLink), and its last warp raises
+    this rank's flag at every rank and waits at most ``wait_s`` for theirs; a
+    rank that does not arrive in time is reported as
+    ``PA_DEVERR_WAIT_TIMEOUT`` (``read_device_errors``) instead of hanging.
+
+    The gathered outputs are two buffers used in turn: another rank may start
+    writing this rank's buffer for call k+2 as soon as this rank's kernel of
+    call k+1 is done, so the tensor returned must be consumed by work ordered
+    on this stream before the next call.  Pass ``out=`` to get the result
+    copied there (on this stream, right after the kernel) for consumers on
+    other streams.  Setup (one collective to swap IPC handles) happens on the
+    first call of a shape, not under a CUDA-graph capture.
+    """
+
+    def __init__(self, group: dist.ProcessGroup | None = None, wait_s: float = 2.0):
+        self.group = group
+        self.wait_ns = int(wait_s * 1e9)
+        self._state: _GatherState | None = None
+        self._calls = 0
+
+    def _setup(self, B, Hq_total, q, D, dtype, device) -> _GatherState:
+        world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
+        key = (B, Hq_total, q, D, dtype, device)
+        out_bytes = B * Hq_total * q * D * torch.tensor([], dtype=dtype).element_size()
+        out_bytes = (out_bytes + 255) // 256 * 256
+        flags_off = 2 * out_bytes
+        blob = torch.zeros(flags_off + max(256, 4 * world), dtype=torch.uint8, device=device)
+        h = _lib.IpcHandle()
+        _lib.check(_lib.load().pa_ipc_export(ctypes.c_void_p(blob.data_ptr()), ctypes.byref(h)), "pa_ipc_export")
+        mine = (bytes(h.bytes), int(h.offset))
+        handles = [None] * world
+        dist.all_gather_object(handles, mine, group=self.group)
+        bases = [blob.data_ptr() if r == rank else _ipc_import(*handles[r]) for r in range(world)]
+        out_ranks = [torch.tensor([b + par * out_bytes for b in bases], dtype=torch.int64, device=device)
+                     for par in (0, 1)]
+        flags_ranks = torch.tensor([b + flags_off for b in bases], dtype=torch.int64, device=device)
+        n = B * Hq_total * q * D
+        outs = [blob[par * out_bytes:par * out_bytes + n * torch.tensor([], dtype=dtype).element_size()]
+                .view(dtype).view(B, Hq_total, q, D) for par in (0, 1)]
+        counters = torch.zeros(2, dtype=torch.int32, device=device)  # epoch, finished warps
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)  # every rank has mapped every buffer before any kernel writes
+        return _GatherState(key, blob, outs, out_ranks, flags_ranks, counters)
+
+    def __call__(self, query, key_cache, value_cache, block_tables, context_lens, scale,
+                 slot_mapping=None, key=None, value=None, **kw) -> torch.Tensor:
+        from .paged_attention import paged_attention_decode
+
+        world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
+        B, hl, q, D = query.shape
+        key_ = (B, hl * world, q, D, query.dtype, query.device)
+        if self._state is None or self._state.key != key_:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("run one fused-gather call of this shape before CUDA-graph capture")
+            self._state = self._setup(*key_)
+            self._calls = 0
+        st = self._state
+        par = self._calls & 1
+        self._calls += 1
+        g = _lib.GatherArgs()
+        g.num_ranks, g.rank, g.head_offset = world, rank, rank * hl
+        g.out_ranks = st.out_ranks[par].data_ptr()
+        g.flags_ranks = st.flags_ranks.data_ptr()
+        g.epoch = st.counters.data_ptr()
+        g.done_warps = st.counters.data_ptr() + 4
+        g.wait_ns = self.wait_ns
+        g.total_heads = hl * world
+        dest = kw.pop("out", None)
+        gathered = st.outs[par]
+        paged_attention_decode(query, key_cache, value_cache, block_tables, context_lens, scale, slot_mapping,
+                               key, value, out=gathered, gather=g, **kw)
+        if dest is None:
+            return gathered
+        if tuple(dest.shape) != tuple(gathered.shape):
+            # HeadShardedDecode's out is the local [B, Hq/N, q, D] block; the
+            # gathered result needs a [B, Hq, q, D] destination
+            raise ValueError("out must be [batch, total query heads, q_len, head_dim]")
+        dest.copy_(gathered)
+        return dest

@@ -54,6 +54,10 @@ int main(void) {
   F(pa_decode_args, workspace_bytes) F(pa_decode_args, allow_overlap_with_previous)
   printf("pa_prefix_groups %zu\n", sizeof(pa_prefix_groups));
   F(pa_prefix_groups, max_prefix_len) F(pa_prefix_groups, member_offsets) F(pa_prefix_groups, seq_group)
+  printf("pa_gather_args %zu\n", sizeof(pa_gather_args));
+  printf("pa_ipc_handle %zu\n", sizeof(pa_ipc_handle));
+  F(pa_gather_args, head_offset) F(pa_gather_args, out_ranks) F(pa_gather_args, flags_ranks)
+  F(pa_gather_args, done_warps) F(pa_gather_args, wait_ns) F(pa_ipc_handle, offset)
   return 0;
 }
 """
@@ -70,8 +74,11 @@ def test_ctypes_structs_match_header_layout(tmp_path):
     assert int(c["pa_kv_append_args"]) == ctypes.sizeof(_lib.KvAppendArgs)
     assert int(c["pa_decode_args"]) == ctypes.sizeof(_lib.DecodeArgs)
     assert int(c["pa_prefix_groups"]) == ctypes.sizeof(_lib.PrefixGroupsArgs)
+    assert int(c["pa_gather_args"]) == ctypes.sizeof(_lib.GatherArgs)
+    assert int(c["pa_ipc_handle"]) == ctypes.sizeof(_lib.IpcHandle)
     classes = {"pa_kv_append_args": _lib.KvAppendArgs, "pa_decode_args": _lib.DecodeArgs,
-               "pa_prefix_groups": _lib.PrefixGroupsArgs}
+               "pa_prefix_groups": _lib.PrefixGroupsArgs, "pa_gather_args": _lib.GatherArgs,
+               "pa_ipc_handle": _lib.IpcHandle}
     for key, val in c.items():
         if "." not in key:
             continue
@@ -110,6 +117,19 @@ def test_cascade_argument_errors_without_a_gpu():
     assert "member_offsets" in _lib.last_error()
     groups.num_groups = -1
     assert lib.pa_decode_cascade(ctypes.byref(args), ctypes.byref(groups), None) == _lib.PA_ERR_INVALID_ARGUMENT
+
+
+def test_gather_argument_errors_without_a_gpu():
+    lib = _lib.load()
+    args = _lib.DecodeArgs()
+    g = _lib.GatherArgs()
+    assert lib.pa_decode_gather(ctypes.byref(args), None, None) == _lib.PA_ERR_INVALID_ARGUMENT
+    g.num_ranks, g.rank = 2, 2
+    assert lib.pa_decode_gather(ctypes.byref(args), ctypes.byref(g), None) == _lib.PA_ERR_INVALID_ARGUMENT
+    g.rank = 1
+    assert lib.pa_decode_gather(ctypes.byref(args), ctypes.byref(g), None) == _lib.PA_ERR_INVALID_ARGUMENT
+    assert "out_ranks" in _lib.last_error()
+    assert lib.pa_ipc_export(None, None) == _lib.PA_ERR_INVALID_ARGUMENT
 
 
 def test_empty_batch_is_a_no_op():

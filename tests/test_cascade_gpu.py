@@ -138,3 +138,26 @@ def test_no_groups_is_the_plain_call():
     args = (q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), 128 ** -0.5)
     assert torch.equal(paged_attention_decode(*args, prefix_groups=pg), paged_attention_decode(*args))
     assert DeviceErrorFlags.PREFIX == 0x10
+
+
+def test_cascade_inside_a_cuda_graph():
+    """One capture of the cascade call replays correctly after the lengths grow
+    (the kernels read lengths, tables and groups on the device)."""
+    from llm_serving_runtime_b200.cuda_graph import DecodeStepGraph
+
+    q, kc, vc, bt, cl, members = _shared_batch([3, 2], [256, 128], 1, [256, 300, 500, 128, 140, 90], 32, 8, 128,
+                                               16, torch.bfloat16, 1, seed=21)
+    B, maxb = bt.shape
+    pg = PrefixGroups.from_members(members, [256, 128], B, DEV)
+    kcd, vcd = kc.to(DEV), vc.to(DEV)
+    graph = DecodeStepGraph([kcd], [vcd], batch=B, max_blocks=maxb, num_q_heads=32, q_len=1, scale=128 ** -0.5,
+                            prefix_groups=pg)
+    for grow in (0, 5):
+        lens = cl - 5 + grow
+        graph.query[0].copy_(q.to(DEV))
+        graph.block_tables.copy_(bt.to(DEV))
+        graph.context_lens.copy_(lens.to(DEV))
+        out = graph.replay()[0]
+        torch.cuda.synchronize()
+        ref = oracle.paged_decode(q, kc, vc, bt, lens, 128 ** -0.5, len_offset=1)
+        assert excess_err(out, ref) <= 0, f"step {grow}: max abs err {max_err(out, ref)}"

@@ -1,0 +1,131 @@
+"""KV-head-sharded decode with the all-gather fused into the decode kernel
+(pa_decode_gather): every output row goes to every rank's gathered output and
+the call ends with a flag exchange whose wait is bounded.
+
+On one GPU the flag words of "other ranks" are plain device buffers: a layout
+of one rank must equal the plain decode bit for bit, and a layout whose second
+rank never raises its flag must report PA_DEVERR_WAIT_TIMEOUT within the bound
+(a failure detected without a fault; the context stays usable).  With two GPUs
+two processes compare the fused gather with the NCCL all-gather and check the
+timeout when one rank skips a call."""
+
+from __future__ import annotations
+
+import dataclasses
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+
+from llm_serving_runtime_b200 import _lib, paged_attention_decode, read_device_errors
+from llm_serving_runtime_b200.paged_attention import DeviceErrorFlags
+from llm_serving_runtime_b200.workloads import SPECS, make_workload
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _args(outs, flags, counters, rank, head_offset, total_heads, wait_ns):
+    g = _lib.GatherArgs()
+    g.num_ranks, g.rank, g.head_offset = len(outs), rank, head_offset
+    g._out_ranks = torch.tensor([o.data_ptr() for o in outs], dtype=torch.int64, device=DEV)
+    g._flags_ranks = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=DEV)
+    g.out_ranks = g._out_ranks.data_ptr()
+    g.flags_ranks = g._flags_ranks.data_ptr()
+    g.epoch = counters.data_ptr()
+    g.done_warps = counters.data_ptr() + 4
+    g.wait_ns = wait_ns
+    g.total_heads = total_heads
+    return g
+
+
+def _workload(batch=48):
+    spec = dataclasses.replace(SPECS["cfg5-llama3-70b"], batch=batch, length_lo=100, length_hi=3000)
+    return make_workload(spec, device=DEV)
+
+
+def test_one_rank_gather_equals_plain_decode():
+    w = _workload()
+    plain = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)
+    out = torch.full_like(plain, float("nan"))
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    counters = torch.zeros(2, dtype=torch.int32, device=DEV)
+    g = _args([out], [flags], counters, 0, 0, plain.shape[1], 2_000_000_000)
+    read_device_errors(DEV)
+    for call in (1, 2):
+        out.fill_(float("nan"))
+        paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                               out=out, gather=g, validate=True)
+        assert torch.equal(out, plain)
+        assert counters.tolist() == [call, 0] and flags.tolist() == [call]
+
+
+def test_missing_rank_times_out_without_a_fault():
+    w = _workload(batch=24)
+    plain = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)
+    B, Hq, q, D = plain.shape
+    outs = [torch.zeros(B, 2 * Hq, q, D, dtype=plain.dtype, device=DEV) for _ in range(2)]
+    flags = [torch.zeros(2, dtype=torch.int32, device=DEV) for _ in range(2)]  # rank 1 never raises its flag
+    counters = torch.zeros(2, dtype=torch.int32, device=DEV)
+    g = _args(outs, flags, counters, 0, 0, 2 * Hq, 50_000_000)  # 50 ms
+    read_device_errors(DEV)
+    paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                           out=outs[0], gather=g)
+    torch.cuda.synchronize()
+    assert read_device_errors(DEV) & DeviceErrorFlags.WAIT_TIMEOUT
+    for o in outs:  # rank 0's rows reached both gathered outputs
+        assert torch.equal(o[:, :Hq], plain)
+    assert flags[1].tolist() == [1, 0] and flags[0].tolist() == [1, 0]
+    again = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                                   validate=True)
+    assert torch.equal(again, plain)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_rank_worker(rank: int, port: int) -> None:
+    import torch.distributed as dist
+
+    from llm_serving_runtime_b200.sharding import FusedHeadGather, HeadShardedDecode, kv_head_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        spec = dataclasses.replace(SPECS["cfg5-llama3-70b"], batch=32, length_lo=100, length_hi=4000)
+        w = make_workload(spec, device=dev, kv_heads=kv_head_range(spec.num_kv_heads, 2, rank))
+        args = (w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)
+        fused, nccl = FusedHeadGather(wait_s=10.0), HeadShardedDecode()
+        for _ in range(3):  # both gathered buffers, twice the first
+            a = fused(*args).clone()
+            b = nccl(*args)
+            assert torch.equal(a, b), f"rank {rank}: fused gather differs from the NCCL all-gather"
+        torch.cuda.synchronize()
+        dist.barrier()
+        # failure detection: rank 1 skips one call, rank 0 reports the timeout
+        short = FusedHeadGather(wait_s=0.2)
+        short(*args)
+        torch.cuda.synchronize()
+        dist.barrier()
+        read_device_errors(dev)
+        if rank == 0:
+            short(*args)
+            torch.cuda.synchronize()
+            assert read_device_errors(dev) & DeviceErrorFlags.WAIT_TIMEOUT
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_ranks_fused_gather_matches_nccl_and_detects_a_missing_rank():
+    import torch.multiprocessing as mp
+
+    mp.spawn(_two_rank_worker, args=(_free_port(),), nprocs=2, join=True)

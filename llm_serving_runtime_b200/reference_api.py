@@ -14,6 +14,12 @@ sm_100a kernel of ``paged_attention.paged_attention_decode``:
   paged_attention_decode                              (:778-802)
   reference_sdpa_attention                            (:805-817, dense helper)
 
+Beyond the reference: ``paged_attention_verify_batched`` attends k draft
+tokens per sequence over the same paged cache in one batched call (causal over
+the drafts).  The reference runs speculative verification one sequence at a
+time outside the batch (worker_server.py:1522) because its batched decode
+accepts only q_len = 1.
+
 Differences on purpose: the output is a fresh tensor, never an alias of a
 cached scratch buffer (the reference returns its fp32 scratch for fp32
 queries, :533-535); long rows are split across the whole batch in one launch
@@ -45,6 +51,7 @@ __all__ = [
     "warmup_paged_attention_kernel",
     "paged_attention_decode_batched",
     "paged_attention_decode",
+    "paged_attention_verify_batched",
     "reference_sdpa_attention",
 ]
 
@@ -139,6 +146,36 @@ def paged_attention_decode_batched(
     return _paged_attention_decode_batched_triton(
         query, k_layer, v_layer, metadata.block_tables, seq_lens, scaling, num_kv_groups
     )
+
+
+def paged_attention_verify_batched(
+    query: torch.Tensor,
+    metadata: PagedDecodeBatchMetadata,
+    num_kv_groups: int,
+    scaling: float,
+    prefix_groups=None,
+) -> torch.Tensor:
+    """Batched speculative verify: ``query [B, heads, k, dim]`` holds each
+    sequence's k draft tokens, whose K/V the cache update already appended, so
+    ``metadata.seq_lens`` counts them.  Draft t of row b attends positions
+    0 .. seq_lens[b] - k + t.  Returns [B, heads, k, dim].  ``prefix_groups``
+    (``prefix_sharing.PrefixGroups``) attends prefixes that rows share through
+    the same blocks once per group."""
+    if query.dim() != 4 or query.shape[0] != metadata.block_tables.shape[0]:
+        raise ValueError("query must be [batch, heads, k, dim] with the batch of block_tables")
+    pool = metadata.pool
+    pool._ensure_pools()
+    k_layer = pool.k_layer_view(metadata.layer_idx)
+    v_layer = pool.v_layer_view(metadata.layer_idx)
+    if query.shape[1] != num_kv_groups * k_layer.shape[1]:
+        raise ValueError("num_heads must equal num_kv_groups * num_kv_heads")
+    if not query.is_cuda:
+        raise RuntimeError("the B200 paged decode needs CUDA tensors (no CPU fallback)")
+    seq_lens = metadata.seq_lens
+    if seq_lens.dtype != torch.int32 or seq_lens.device != query.device:
+        seq_lens = seq_lens.to(device=query.device, dtype=torch.int32)
+    return _decode(query, k_layer, v_layer, metadata.block_tables, seq_lens, scaling,
+                   context_lens_include_new=True, prefix_groups=prefix_groups)
 
 
 def paged_attention_decode(

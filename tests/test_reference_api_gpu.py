@@ -141,3 +141,35 @@ def test_triton_available_and_warmup():
     pool = GpuKVBlockPool(num_blocks=4, block_size_tokens=16, num_layers=1, num_kv_heads=2, head_dim=128,
                           dtype=torch.bfloat16, device=DEV)
     ra.warmup_paged_attention_kernel(pool, num_heads=8, num_kv_groups=4, head_dim=128, block_ids=[0, 1])
+
+
+def test_batched_speculative_verify_through_the_pool():
+    """k = 4 draft tokens per sequence appended with write_tokens_batch (as the
+    batched cache update does), then verified in one batched call: causal over
+    the drafts, against the oracle."""
+    dtype, Hkv, G, D, bs, k = torch.bfloat16, 8, 4, 128, 16, 4
+    cached = [5, 60, 333, 1000, 16]
+    B = len(cached)
+    nmax = math.ceil((max(cached) + k) / bs)
+    pool = GpuKVBlockPool(num_blocks=B * nmax + 1, block_size_tokens=bs, num_layers=2, num_kv_heads=Hkv,
+                          head_dim=D, dtype=dtype, device=DEV)
+    g = torch.Generator(device="cpu").manual_seed(7)
+    perm = torch.randperm(B * nmax + 1, generator=g)[: B * nmax].view(B, nmax).to(torch.int32)
+    tables = perm.to(DEV)
+    for b, c in enumerate(cached):  # the cached context of each row, layer 1
+        kk = torch.randn(1, Hkv, c, D, generator=g).to(dtype).to(DEV)
+        vv = torch.randn(1, Hkv, c, D, generator=g).to(dtype).to(DEV)
+        pool.write_tokens(1, perm[b].tolist(), 0, kk, vv)
+    new_k = torch.randn(B, Hkv, k, D, generator=g).to(dtype).to(DEV)
+    new_v = torch.randn(B, Hkv, k, D, generator=g).to(dtype).to(DEV)
+    pool.write_tokens_batch(1, tables, torch.tensor(cached, device=DEV), new_k, new_v)
+    query = torch.randn(B, Hkv * G, k, D, generator=g).to(dtype).to(DEV)
+    seq_lens = torch.tensor(cached, dtype=torch.int32, device=DEV) + k
+    meta = ra.PagedDecodeBatchMetadata(pool=pool, layer_idx=1, block_tables=tables, seq_lens=seq_lens)
+    out = ra.paged_attention_verify_batched(query, meta, G, D ** -0.5)
+    assert out.shape == (B, Hkv * G, k, D)
+    ref = oracle.paged_decode(query.cpu(), pool.k_layer_view(1).cpu(), pool.v_layer_view(1).cpu(), perm,
+                              seq_lens.cpu(), D ** -0.5, len_offset=0)
+    assert excess_err(out, ref) <= 0
+    with pytest.raises(ValueError, match="num_heads"):
+        ra.paged_attention_verify_batched(query, meta, G + 1, D ** -0.5)

@@ -3,6 +3,7 @@
 from __future__ import annotations
 
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -61,6 +62,9 @@ def _files(name: str) -> list[str]:
 
 
 def reference_root() -> Path | None:
-    """The reference checkout when it is mounted (only in the build container)."""
-    p = Path("/root/reference")
+    """The reference checkout named by LLM_SERVING_RUNTIME_ROOT, when it exists."""
+    root = os.environ.get("LLM_SERVING_RUNTIME_ROOT")
+    if not root:
+        return None
+    p = Path(root)
     return p if (p / "runtime" / "phase2" / "paged_attention_triton.py").exists() else None

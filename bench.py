@@ -157,12 +157,15 @@ def run_reference(args) -> None:
     spec = SPECS[args.workload]
     if args.batch:
         spec = dataclasses.replace(spec, batch=args.batch)
-    GB = spec.batch * world
-    lens_all = sample_lengths(spec, GB)
+    # The job our arm runs at this N: the one-GPU workload on every rank
+    # (sequence sharding), or the one workload split by KV heads.
+    copies = 1 if _shard_mode(args, world) == "head" else world
+    GB = spec.batch * copies
+    lens_one = sample_lengths(spec, spec.batch)
     g = torch.Generator().manual_seed(4242)
-    n_sample = min(args.cpu_rows, GB)
-    rows = sorted(torch.randperm(GB, generator=g)[:n_sample].tolist())
-    w = make_workload(spec, device="cpu", rows=rows, global_batch=GB)
+    n_sample = min(args.cpu_rows, spec.batch)
+    rows = sorted(torch.randperm(spec.batch, generator=g)[:n_sample].tolist())
+    w = make_workload(spec, device="cpu", rows=rows, global_batch=spec.batch)
     threads = os.cpu_count() or 1
     kc, vc = w.key_cache.clone(), w.value_cache.clone()
 
@@ -176,9 +179,9 @@ def run_reference(args) -> None:
     for _ in range(args.steps):
         step()
     dt = (time.perf_counter() - t0) / args.steps
-    # scale the sample's time to the whole batch by attended tokens
-    L_all = float((lens_all + spec.q_len).sum())
-    L_smp = float((lens_all[rows] + spec.q_len).sum())
+    # scale the sample's time to the whole job by attended tokens
+    L_all = copies * float((lens_one + spec.q_len).sum())
+    L_smp = float((lens_one[rows] + spec.q_len).sum())
     t_full = dt * L_all / L_smp
     value = GB * spec.q_len / t_full
     sample = (f"{n_sample} of {GB} sequences of {args.workload} (seeded), append + decode per step; "
@@ -196,6 +199,13 @@ def run_reference(args) -> None:
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _shard_mode(args, world: int) -> str:
+    """Multi-GPU layout: KV heads for config 5 at N > 1 (auto), sequences otherwise."""
+    if args.shard != "auto":
+        return args.shard
+    return "head" if (world > 1 and args.workload == "cfg5-llama3-70b") else "seq"
 
 
 def main() -> None:
@@ -229,10 +239,8 @@ def main() -> None:
     import torch.distributed as dist
 
     from llm_serving_runtime_b200 import _lib, paged_attention_decode
-    from llm_serving_runtime_b200.sharding import FusedHeadGather, HeadShardedDecode, kv_head_range, \
-        shard_sequences
-    from llm_serving_runtime_b200.workloads import SPECS, algorithmic_bytes, attention_flops, make_workload, \
-        sample_lengths
+    from llm_serving_runtime_b200.sharding import FusedHeadGather, HeadShardedDecode, kv_head_range
+    from llm_serving_runtime_b200.workloads import SPECS, algorithmic_bytes, attention_flops, make_workload
 
     world, rank, local = _dist_setup()
     if world != args.gpus:
@@ -245,20 +253,18 @@ def main() -> None:
     spec = SPECS[args.workload]
     if args.batch:
         spec = dataclasses.replace(spec, batch=args.batch)
-    shard = args.shard
-    if shard == "auto":
-        shard = "head" if (world > 1 and args.workload == "cfg5-llama3-70b") else "seq"
+    shard = _shard_mode(args, world)
     if shard == "head":
         # every rank holds its KV heads of the whole batch; outputs all-gathered
         GB = spec.batch
         w = make_workload(spec, device=dev, kv_heads=kv_head_range(spec.num_kv_heads, world, rank))
         gather = FusedHeadGather() if args.gather == "fused" else HeadShardedDecode()
     else:
+        # Weak scaling with the per-GPU work fixed: every rank holds the one-GPU
+        # workload itself (its lengths and prefix groups) with its own block
+        # placement and data.
         GB = spec.batch * world
-        lens = sample_lengths(spec, GB) + spec.q_len
-        group = spec.batch // spec.prefix_groups if spec.length_dist == "prefix" else 0
-        shards = shard_sequences(lens.tolist(), world, group_size=group)
-        w = make_workload(spec, device=dev, rows=shards[rank], global_batch=GB)
+        w = make_workload(spec, device=dev, seed_offset=rank)
         gather = None
     B, q = w.batch, w.q_len
     out = torch.empty_like(w.query)
@@ -319,7 +325,11 @@ def main() -> None:
         barrier()
     local_ms = ev0.elapsed_time(ev1)
     t = torch.tensor([local_ms], device=dev, dtype=torch.float64)
+    rank_ms = [local_ms / args.steps]
     if world > 1:
+        every = torch.empty(world, device=dev, dtype=torch.float64)
+        dist.all_gather_into_tensor(every, t)
+        rank_ms = [v / args.steps for v in every.tolist()]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
@@ -343,6 +353,11 @@ def main() -> None:
         ends[i].record(stream)
     torch.cuda.synchronize()
     dec_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    dec_ms_by_rank = [dec_ms]
+    if world > 1:
+        every = torch.empty(world, device=dev, dtype=torch.float64)
+        dist.all_gather_into_tensor(every, torch.tensor([dec_ms], device=dev, dtype=torch.float64))
+        dec_ms_by_rank = every.tolist()
     dec_kernel = _lib.last_kernel()
     # A block shared by several sequences (config 4's prefixes) is counted once:
     # the minimum bytes the call must move.  The per-sequence (logical) figure
@@ -488,6 +503,8 @@ def main() -> None:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "overlap": "2 copy streams, double-buffered", "result_matches_device_run": ok},
         "gpu_launches": gpu_launches,
+        "ms_per_step_by_rank": [round(v, 5) for v in rank_ms],
+        "kernel_ms_by_rank": [round(v, 5) for v in dec_ms_by_rank],
         "clocks": clk,
     }
     if cpu is not None:

@@ -85,8 +85,10 @@ class HeadShardedDecode:
 
 
 # Peer allocations mapped into this process, by IPC handle: an allocation is
-# opened once however many buffers inside it are shared.
+# opened once however many buffers inside it are shared, and released when the
+# last user lets it go.
 _ipc_bases: dict[bytes, int] = {}
+_ipc_users: dict[bytes, int] = {}
 
 
 def _ipc_import(handle_bytes: bytes, offset: int) -> int:
@@ -99,13 +101,22 @@ def _ipc_import(handle_bytes: bytes, offset: int) -> int:
         _lib.check(_lib.load().pa_ipc_import(ctypes.byref(h), ctypes.byref(ptr)), "pa_ipc_import")
         base = int(ptr.value)
         _ipc_bases[handle_bytes] = base
+    _ipc_users[handle_bytes] = _ipc_users.get(handle_bytes, 0) + 1
     return base + offset
 
 
+def _ipc_drop(handle_bytes: bytes) -> None:
+    _ipc_users[handle_bytes] -= 1
+    if _ipc_users[handle_bytes] == 0:
+        _lib.check(_lib.load().pa_ipc_release(ctypes.c_void_p(_ipc_bases.pop(handle_bytes))), "pa_ipc_release")
+        del _ipc_users[handle_bytes]
+
+
 class _GatherState:
-    def __init__(self, key, blob, outs, out_ranks, flags_ranks, counters):
+    def __init__(self, key, blob, outs, out_ranks, flags_ranks, counters, peer_handles):
         self.key, self.blob, self.outs = key, blob, outs
         self.out_ranks, self.flags_ranks, self.counters = out_ranks, flags_ranks, counters
+        self.peer_handles = peer_handles  # IPC handles of the other ranks' allocations
 
 
 class FusedHeadGather:
@@ -134,6 +145,18 @@ class FusedHeadGather:
         self.wait_ns = int(wait_s * 1e9)
         self._state: _GatherState | None = None
         self._calls = 0
+        self._unfused = HeadShardedDecode(group=group)  # fp32: the kernel fuses fp16 / bf16 only
+
+    def close(self) -> None:
+        """Release the peer mappings and buffers (collective: every rank calls it
+        after its last call; a barrier makes sure no rank still writes)."""
+        if self._state is None:
+            return
+        torch.cuda.synchronize(self._state.blob.device)
+        dist.barrier(group=self.group)
+        for hb in self._state.peer_handles:
+            _ipc_drop(hb)
+        self._state = None
 
     def _setup(self, B, Hq_total, q, D, dtype, device) -> _GatherState:
         world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
@@ -148,6 +171,7 @@ class FusedHeadGather:
         handles = [None] * world
         dist.all_gather_object(handles, mine, group=self.group)
         bases = [blob.data_ptr() if r == rank else _ipc_import(*handles[r]) for r in range(world)]
+        peer_handles = [handles[r][0] for r in range(world) if r != rank]
         out_ranks = [torch.tensor([b + par * out_bytes for b in bases], dtype=torch.int64, device=device)
                      for par in (0, 1)]
         flags_ranks = torch.tensor([b + flags_off for b in bases], dtype=torch.int64, device=device)
@@ -157,18 +181,24 @@ class FusedHeadGather:
         counters = torch.zeros(2, dtype=torch.int32, device=device)  # epoch, finished warps
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)  # every rank has mapped every buffer before any kernel writes
-        return _GatherState(key, blob, outs, out_ranks, flags_ranks, counters)
+        return _GatherState(key, blob, outs, out_ranks, flags_ranks, counters, peer_handles)
 
     def __call__(self, query, key_cache, value_cache, block_tables, context_lens, scale,
                  slot_mapping=None, key=None, value=None, **kw) -> torch.Tensor:
         from .paged_attention import paged_attention_decode
 
+        if query.dtype == torch.float32:
+            dest = kw.pop("out", None)
+            res = self._unfused(query, key_cache, value_cache, block_tables, context_lens, scale,
+                                slot_mapping, key, value, **kw)
+            return res if dest is None else dest.copy_(res)
         world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
         B, hl, q, D = query.shape
         key_ = (B, hl * world, q, D, query.dtype, query.device)
         if self._state is None or self._state.key != key_:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("run one fused-gather call of this shape before CUDA-graph capture")
+            self.close()  # a new shape on every rank at once: drop the old buffers together
             self._state = self._setup(*key_)
             self._calls = 0
         st = self._state

@@ -107,8 +107,14 @@ def _two_rank_worker(rank: int, port: int) -> None:
             a = fused(*args).clone()
             b = nccl(*args)
             assert torch.equal(a, b), f"rank {rank}: fused gather differs from the NCCL all-gather"
+        dest = torch.empty_like(b)
+        assert fused(*args, out=dest) is dest and torch.equal(dest, b)
+        # fp32 takes the NCCL form under the same call
+        args32 = (w.query.float(), w.key_cache.float(), w.value_cache.float()) + args[3:]
+        assert torch.allclose(fused(*args32), nccl(*args32))
         torch.cuda.synchronize()
         dist.barrier()
+        fused.close()
         # failure detection: rank 1 skips one call, rank 0 reports the timeout
         short = FusedHeadGather(wait_s=0.2)
         short(*args)
@@ -120,6 +126,7 @@ def _two_rank_worker(rank: int, port: int) -> None:
             torch.cuda.synchronize()
             assert read_device_errors(dev) & DeviceErrorFlags.WAIT_TIMEOUT
         dist.barrier()
+        short.close()
     finally:
         dist.destroy_process_group()
 

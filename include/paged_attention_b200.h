@@ -143,6 +143,10 @@ PA_API int pa_kv_append(const pa_kv_append_args* args, void* stream);
 
 /* Paged decode attention (split-K over the whole batch with an in-kernel
  * log-sum-exp merge).  fp16/bf16 use tensor-core tiles; fp32 stays on CUDA cores.
+ * head_dim: fp16/bf16 any multiple of 8 up to 128 (tiles of 64 or 128 columns,
+ * the columns past head_dim zero-filled by TMA), fp32 any value up to 128; the
+ * reference's kernels take any head_dim (a power-of-two tile with a mask,
+ * paged_attention_triton.py:497).  Others return PA_ERR_UNSUPPORTED.
  * Replaces: paged_attention_decode_batched -> _paged_attention_decode_batched_triton,
  * runtime/phase2/paged_attention_triton.py:460-552 and :745-775, with the kernels at
  * :148-243 (direct batched), :245-336 (split), :338-412 (direct single) and

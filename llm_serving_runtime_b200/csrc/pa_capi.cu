@@ -160,6 +160,16 @@ int multiquery_policy() {
   return policy;
 }
 
+// The kernels' padded head width for a head_dim: the 16-bit tensor-core
+// kernels tile 64 or 128 columns (TMA zero-fills the columns past the real
+// head_dim), the fp32 kernel 32, 64 or 128.  0 when the head_dim is not served.
+int padded_head_dim(int head_dim, int dtype) {
+  if (head_dim <= 0) return 0;
+  if (dtype == PA_DTYPE_FLOAT32) return head_dim <= 32 ? 32 : head_dim <= 64 ? 64 : head_dim <= 128 ? 128 : 0;
+  if (head_dim % 8 != 0) return 0;  // rows of 16-byte pieces
+  return head_dim <= 64 ? 64 : head_dim <= 128 ? 128 : 0;
+}
+
 struct DecodeShape {
   int G, GQ, NMG, slot_rows;
 };
@@ -243,7 +253,9 @@ size_t pa_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num
   if (device_info(device, &info) != PA_OK) return 0;
   const DecodeShape s = decode_shape(num_q_heads, num_kv_heads, q_len);
   if (dtype == PA_DTYPE_FLOAT32) return pa::kWsHeaderBytes;
-  return workspace_bytes_impl(s.slot_rows, head_dim, info->num_sms * pa::kDecodeWarps);
+  const int DP = padded_head_dim(head_dim, dtype);
+  if (DP == 0) return pa::kWsHeaderBytes;  // not served: pa_decode itself reports it
+  return workspace_bytes_impl(s.slot_rows, DP, info->num_sms * pa::kDecodeWarps);
 }
 
 int pa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
@@ -339,7 +351,7 @@ size_t pa_cascade_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t nu
   if (device_info(device, &info) != PA_OK) return 0;
   const DecodeShape s = decode_shape(num_q_heads, num_kv_heads, q_len);
   const CascadeShape c = cascade_shape(info->num_sms, num_groups, max_members, max_prefix_len, num_kv_heads, s.GQ,
-                                       (long long)batch * num_q_heads * q_len, head_dim);
+                                       (long long)batch * num_q_heads * q_len, padded_head_dim(head_dim, dtype));
   return base + c.ml_bytes + c.acc_bytes + c.cnt_bytes;
 }
 
@@ -436,12 +448,16 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, con
   if (st != PA_OK) return st;
   if (a->key_cache.num_blocks != a->value_cache.num_blocks)
     return fail(PA_ERR_INVALID_ARGUMENT, "key_cache and value_cache must have the same number of blocks");
-  const int D = a->head_dim, bs = a->block_size;
+  const int Dv = a->head_dim, bs = a->block_size;
+  const int D = padded_head_dim(Dv, dtype);  // the kernels' tile width
+  if (D == 0)
+    return fail(PA_ERR_UNSUPPORTED, "head_dim %d not served (%s)", Dv,
+                dtype == PA_DTYPE_FLOAT32 ? "fp32: up to 128" : "fp16/bf16: a multiple of 8 up to 128");
   if ((int64_t)a->max_blocks * bs > (int64_t)1 << 30)
     return fail(PA_ERR_UNSUPPORTED, "max_blocks * block_size too large");
   if (!aligned_ptr(a->query, 4) || !aligned_ptr(a->out, 4) ||
-      ((a->query_stride_b | a->query_stride_h | a->query_stride_t | a->out_stride_b |
-        a->out_stride_h | a->out_stride_t) & 1) != 0)
+      (dtype != PA_DTYPE_FLOAT32 && ((a->query_stride_b | a->query_stride_h | a->query_stride_t |
+                                      a->out_stride_b | a->out_stride_h | a->out_stride_t) & 1) != 0))
     return fail(PA_ERR_UNSUPPORTED, "query/out rows must be 4-byte aligned");
   if (a->workspace == nullptr || a->workspace_bytes < pa::kWsHeaderBytes)
     return fail(PA_ERR_WORKSPACE, "a workspace of pa_decode_workspace_bytes() bytes is required");
@@ -487,6 +503,7 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, con
   p.NMG = s.NMG;
   p.bs = bs;
   p.D = D;
+  p.Dv = Dv;
   p.scale = a->scale;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.status = static_cast<uint32_t*>(a->workspace);
@@ -495,8 +512,6 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, con
   cudaStream_t strm = static_cast<cudaStream_t>(stream);
 
   if (dtype == PA_DTYPE_FLOAT32) {
-    if (D != 32 && D != 64 && D != 128)
-      return fail(PA_ERR_UNSUPPORTED, "fp32 decode supports head_dim 32/64/128, got %d", D);
     if (!aligned_ptr(a->key_cache.data, 4) || !aligned_ptr(a->value_cache.data, 4))
       return fail(PA_ERR_UNSUPPORTED, "cache base must be 4-byte aligned");
     g_last_kernel = "pa::decode_f32_kernel";
@@ -506,8 +521,6 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, con
   }
 
   // fp16 / bf16: tensor-core kernel.
-  if (D != 64 && D != 128)
-    return fail(PA_ERR_UNSUPPORTED, "fp16/bf16 decode supports head_dim 64/128, got %d", D);
   if (bs < 8 || bs > 256 || (bs & (bs - 1)) != 0)
     return fail(PA_ERR_UNSUPPORTED, "fp16/bf16 decode needs a power-of-two block_size in [8, 256], got %d", bs);
   const int grid = info->num_sms;
@@ -570,9 +583,10 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, con
   const size_t smem = pa::decode_mma_smem_bytes(D, p.B, stages, cascade);
 
   CUtensorMap tmk, tmv;
-  st = encode_cache_map(&tmk, a->key_cache, dtype, D, bs, p.Hkv, "key_cache");
+  // the maps' rows are the real head_dim: TMA fills the columns past it with zeros
+  st = encode_cache_map(&tmk, a->key_cache, dtype, Dv, bs, p.Hkv, "key_cache");
   if (st != PA_OK) return st;
-  st = encode_cache_map(&tmv, a->value_cache, dtype, D, bs, p.Hkv, "value_cache");
+  st = encode_cache_map(&tmv, a->value_cache, dtype, Dv, bs, p.Hkv, "value_cache");
   if (st != PA_OK) return st;
 
   {

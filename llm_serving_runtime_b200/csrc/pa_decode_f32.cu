@@ -76,8 +76,10 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const Decode
       const int r = i / D, d = i - (i / D) * D;
       const int qr = r0 + r;
       const int g = qr / p.q_len, t = qr - (qr / p.q_len) * p.q_len;
-      s_q[r * D + d] = static_cast<const float*>(p.q)[(long long)b * p.q_sb + (long long)(h * p.G + g) * p.q_sh +
-                                                     (long long)t * p.q_st + d];
+      s_q[r * D + d] = d < p.Dv ? static_cast<const float*>(p.q)[(long long)b * p.q_sb +
+                                                                  (long long)(h * p.G + g) * p.q_sh +
+                                                                  (long long)t * p.q_st + d]
+                                : 0.f;
     }
     __syncthreads();
 
@@ -109,6 +111,7 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const Decode
         for (int t = 0; t < cnt; ++t) {
 #pragma unroll
           for (int j = 0; j < DPL; ++j) {
+            if (lane + 32 * j >= p.Dv) break;  // no read past the row; those columns are never used
             cp_async_4(smem_addr(&s_k[t * PITCH + lane + 32 * j]), kb + (long long)(c0 + t) * p.k_st + lane + 32 * j);
             cp_async_4(smem_addr(&s_v[t * PITCH + lane + 32 * j]), vb + (long long)(c0 + t) * p.v_st + lane + 32 * j);
           }
@@ -122,7 +125,7 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const Decode
         if (lane < cnt) {
           const float* kr = s_k + lane * PITCH;
 #pragma unroll 4
-          for (int d = 0; d < D; ++d) {
+          for (int d = 0; d < p.Dv; ++d) {
             const float kd = kr[d];
 #pragma unroll
             for (int r = 0; r < kF32Rows; ++r)
@@ -190,6 +193,7 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_kernel(const Decode
     __syncthreads();
     for (int i = threadIdx.x; i < R * D; i += blockDim.x) {
       const int r = i / D, d = i - (i / D) * D;
+      if (d >= p.Dv) continue;  // columns past the head_dim
       float M = -INFINITY;
       for (int w = 0; w < kF32Warps; ++w) M = fmaxf(M, s_ml[(w * 2) * kF32Rows + r]);
       float lsum = 0.f, a = 0.f;

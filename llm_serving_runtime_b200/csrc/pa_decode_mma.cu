@@ -229,8 +229,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
             const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
             v = pack2<T>(a.x * inv, a.y * inv);
           }
-          for (int dst = 0; dst < n_dst; ++dst)
-            *reinterpret_cast<uint32_t*>(out_row(dst, b, h * p.G + g, t) + 2 * d2) = v;
+          if (2 * d2 < p.Dv)
+            for (int dst = 0; dst < n_dst; ++dst)
+              *reinterpret_cast<uint32_t*>(out_row(dst, b, h * p.G + g, t) + 2 * d2) = v;
         }
       }
     }
@@ -422,7 +423,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
               (long long)(h * p.G + g) * p.q_sh + (long long)t * p.q_st;
         lim1 = L - p.q_len + t;
       }
-      load_query_frags<T, D>(qa, qp0, qp1, quad);
+      load_query_frags<T, D>(qa, qp0, qp1, quad, p.Dv);
 #pragma unroll
       for (int nd = 0; nd < NDT; ++nd) {
         o_acc[nd][0] = o_acc[nd][1] = o_acc[nd][2] = o_acc[nd][3] = 0.f;
@@ -481,14 +482,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           for (int dst = 0; dst < n_dst; ++dst)
             store_rows<T, D>(r0_ok ? out_row(dst, b, h * p.G + qa0 % p.G, qa0 / p.G) : nullptr,
                              r1_ok ? out_row(dst, b, h * p.G + qa1 % p.G, qa1 / p.G) : nullptr, o_acc, lt0, lt1,
-                             quad);
+                             quad, p.Dv);
         } else if (cascade && s_u0[b] > 0) {
           const long long rb = (long long)b * p.Hq + h * p.G;
           const long long ridx0 = (rb + qa0 % p.G) * p.q_len + qa0 / p.G;
           const long long ridx1 = (rb + qa1 % p.G) * p.q_len + qa1 / p.G;
           store_rows_folded<T, D>(op0, op1, o_acc, m0, m1, lt0, lt1, ridx0, ridx1, p, quad);
         } else {
-          store_rows<T, D>(op0, op1, o_acc, lt0, lt1, quad);
+          store_rows<T, D>(op0, op1, o_acc, lt0, lt1, quad, p.Dv);
         }
       } else {
         // Partial: (m, l, acc) to this warp's slot, then count the arrival.
@@ -618,7 +619,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
                 for (int dst = 0; dst < n_dst; ++dst) {
                   T* op = out_row(dst, b, h * p.G + g, t);
 #pragma unroll
-                  for (int k = 0; k < DPL; ++k) op[lane + 32 * k] = from_float<T>(acc[r][k] * inv);
+                  for (int k = 0; k < DPL; ++k)
+                    if (lane + 32 * k < p.Dv) op[lane + 32 * k] = from_float<T>(acc[r][k] * inv);
                 }
               }
             }

@@ -43,7 +43,8 @@ struct DecodeParams {
   int32_t len_offset;
   void* out;
   int64_t o_sb, o_sh, o_st;
-  int32_t B, q_len, Hq, Hkv, G, GQ, NMG, bs, D;
+  int32_t B, q_len, Hq, Hkv, G, GQ, NMG, bs, D;  // D: the kernels' padded head width (tile layout)
+  int32_t Dv;        // the real head_dim (<= D): columns at or past it are masked
   float scale;       // softmax scale
   float scale_log2;  // scale * log2(e)
   uint32_t* status;  // device error word

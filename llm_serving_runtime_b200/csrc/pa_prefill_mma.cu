@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   const int mask_from = L - p.q_len + (row0 + warp * 16) / p.G;
 
   uint32_t qa[D / 16][4];
-  load_query_frags<T, D>(qa, qp0, qp1, quad);
+  load_query_frags<T, D>(qa, qp0, qp1, quad, p.Dv);
   float o_acc[D / 8][4];
 #pragma unroll
   for (int nd = 0; nd < D / 8; ++nd) o_acc[nd][0] = o_acc[nd][1] = o_acc[nd][2] = o_acc[nd][3] = 0.f;
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   float lt1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
   lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
   lt1 += __shfl_xor_sync(0xffffffffu, lt1, 2);
-  store_rows<T, D>(op0, op1, o_acc, lt0, lt1, quad);
+  store_rows<T, D>(op0, op1, o_acc, lt0, lt1, quad, p.Dv);
 }
 
 size_t prefill_smem_bytes(int D) {

@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (row_ok) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
+        if (row_ok && c * 8 < p.Dv) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
         *reinterpret_cast<uint4*>(qt + (c >> 3) * 16384 + sw128_chunk(r, c & 7)) = v;
       }
     }
@@ -664,6 +664,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         if (row_ok) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
+            if (c0 + i >= p.Dv) break;  // columns past the head_dim
             uint4 v;
             v.x = pack2<T>(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
             v.y = pack2<T>(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);

@@ -56,17 +56,19 @@ __device__ __forceinline__ float hi_half<__half>(uint32_t v) {
 }
 
 // Query fragments (A operand) of the warp's 16 rows; a null row pointer gives
-// a zero (padding) row.
+// a zero (padding) row, and columns at or past the head_dim Dv (a multiple of
+// 8, <= D) are zero.
 template <typename T, int D>
 __device__ __forceinline__ void load_query_frags(uint32_t (&qa)[D / 16][4], const T* qp0, const T* qp1,
-                                                 int quad) {
+                                                 int quad, int Dv) {
 #pragma unroll
   for (int ks = 0; ks < D / 16; ++ks) {
     const int d = ks * 16 + 2 * quad;
-    qa[ks][0] = qp0 ? __ldg(reinterpret_cast<const unsigned int*>(qp0 + d)) : 0u;
-    qa[ks][1] = qp1 ? __ldg(reinterpret_cast<const unsigned int*>(qp1 + d)) : 0u;
-    qa[ks][2] = qp0 ? __ldg(reinterpret_cast<const unsigned int*>(qp0 + d + 8)) : 0u;
-    qa[ks][3] = qp1 ? __ldg(reinterpret_cast<const unsigned int*>(qp1 + d + 8)) : 0u;
+    const bool lo = d < Dv, hi = d + 8 < Dv;
+    qa[ks][0] = (qp0 && lo) ? __ldg(reinterpret_cast<const unsigned int*>(qp0 + d)) : 0u;
+    qa[ks][1] = (qp1 && lo) ? __ldg(reinterpret_cast<const unsigned int*>(qp1 + d)) : 0u;
+    qa[ks][2] = (qp0 && hi) ? __ldg(reinterpret_cast<const unsigned int*>(qp0 + d + 8)) : 0u;
+    qa[ks][3] = (qp1 && hi) ? __ldg(reinterpret_cast<const unsigned int*>(qp1 + d + 8)) : 0u;
   }
 }
 
@@ -194,15 +196,17 @@ __device__ __forceinline__ void attend_unit(uint32_t kbase, uint32_t vbase, cons
   }
 }
 
-// Normalise and store the warp's rows (row pointers may be null for padding rows).
+// Normalise and store the warp's rows (row pointers may be null for padding
+// rows); columns at or past the head_dim Dv are not stored.
 template <typename T, int D>
 __device__ __forceinline__ void store_rows(T* op0, T* op1, const float (&o_acc)[D / 8][4], float l0, float l1,
-                                           int quad) {
+                                           int quad, int Dv) {
   const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
   const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
 #pragma unroll
   for (int nd = 0; nd < D / 8; ++nd) {
     const int d = nd * 8 + 2 * quad;
+    if (d >= Dv) break;
     if (op0) *reinterpret_cast<uint32_t*>(op0 + d) = pack2<T>(o_acc[nd][0] * inv0, o_acc[nd][1] * inv0);
     if (op1) *reinterpret_cast<uint32_t*>(op1 + d) = pack2<T>(o_acc[nd][2] * inv1, o_acc[nd][3] * inv1);
   }
@@ -238,7 +242,7 @@ __device__ __forceinline__ void store_rows_folded(T* op0, T* op1, float (&o_acc)
     o_acc[nd][2] = fmaf(o_acc[nd][2], w1, v1 * x1.x);
     o_acc[nd][3] = fmaf(o_acc[nd][3], w1, v1 * x1.y);
   }
-  store_rows<T, D>(op0, op1, o_acc, l0, l1, quad);
+  store_rows<T, D>(op0, op1, o_acc, l0, l1, quad, p.Dv);
 }
 
 }  // namespace pa

@@ -70,6 +70,7 @@ CASES = [
     ([6], [512], 0, [512] * 6, 32, 8, 128, 32, torch.bfloat16, 4),                 # suffix = new tokens only
     ([2, 2], [128, 96], 1, [128, 300, 96, 97, 10], 8, 2, 128, 16, torch.bfloat16, 1),
     ([3], [256], 0, [300, 256, 999], 64, 8, 128, 16, torch.bfloat16, 2),           # G = 8
+    ([3, 2], [256, 128], 1, [256, 300, 500, 128, 200, 60], 32, 8, 80, 16, torch.bfloat16, 2),  # head_dim 80
 ]
 
 

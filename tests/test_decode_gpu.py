@@ -152,6 +152,44 @@ def test_edge_shapes_vs_oracle(B, Hq, Hkv, D, bs, dtype, lens, q_len):
     assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"
 
 
+HEAD_DIMS = [
+    # head_dim the reference's kernels serve (any size, padded to a power of
+    # two) but the tiles do not match: the 16-bit kernels pad to 64 / 128 and
+    # the fp32 kernel to 32 / 64 / 128 (B, Hq, Hkv, D, bs, dtype, lens, q_len)
+    (4, 32, 8, 80, 16, torch.bfloat16, [1, 100, 1000, 3000], 1),
+    (4, 14, 2, 96, 16, torch.float16, [7, 64, 500, 2047], 1),
+    (3, 16, 4, 112, 8, torch.bfloat16, [15, 300, 999], 4),
+    (3, 8, 2, 32, 16, torch.bfloat16, [3, 200, 1500], 1),
+    (3, 8, 2, 40, 32, torch.float16, [33, 64, 700], 2),
+    (3, 8, 8, 48, 16, torch.bfloat16, [0, 17, 640], 1),
+    (3, 8, 2, 80, 16, torch.float32, [5, 100, 900], 1),
+    (3, 8, 2, 100, 16, torch.float32, [1, 63, 400], 2),
+    (2, 4, 2, 24, 4, torch.float32, [7, 30], 1),
+    (2, 2, 2, 1, 4, torch.float32, [3, 12], 1),     # a one-dimensional head
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,bs,dtype,lens,q_len", HEAD_DIMS)
+def test_other_head_dims_vs_oracle(B, Hq, Hkv, D, bs, dtype, lens, q_len):
+    q, kc, vc, bt, cl = _synthetic(B, Hq, Hkv, D, bs, dtype, lens, q_len, seed=B * 11 + D)
+    nk, nv = torch.randn(B, Hkv, q_len, D).to(dtype), torch.randn(B, Hkv, q_len, D).to(dtype)
+    kcd, vcd = kc.to(DEV), vc.to(DEV)
+    out = paged_attention_decode(q.to(DEV), kcd, vcd, bt.to(DEV), cl.to(DEV), D ** -0.5, None, nk.to(DEV),
+                                 nv.to(DEV), validate=True)
+    kc2, vc2 = kc.clone(), vc.clone()
+    oracle.write_tokens_batch(kc2.unsqueeze(1), vc2.unsqueeze(1), 0, bt, cl.long(), nk, nv)
+    assert torch.equal(kcd.cpu(), kc2) and torch.equal(vcd.cpu(), vc2)  # the append, bit for bit
+    ref = oracle.paged_decode(q, kc2, vc2, bt, cl, D ** -0.5)
+    assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"
+
+
+def test_unserved_head_dims_are_value_errors():
+    for D, dtype in ((136, torch.bfloat16), (256, torch.float16), (20, torch.bfloat16), (160, torch.float32)):
+        q, kc, vc, bt, cl = _synthetic(1, 2, 2, D, 16, dtype, [5], seed=3)
+        with pytest.raises(ValueError, match="head_dim"):
+            paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), 0.1)
+
+
 def test_one_long_sequence_split_over_the_whole_grid():
     # B = 1, 64k tokens: every warp of the grid takes a slice of the one row,
     # so the log-sum-exp merge combines hundreds of partials.

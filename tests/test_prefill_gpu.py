@@ -32,6 +32,9 @@ CASES = [
     (12, 14, 2, 64, 16, torch.float16, [1, 2, 3, 900, 100, 0, 33, 64, 65, 500, 8, 1200], 640),
     (6, 32, 8, 128, 8, torch.bfloat16, [3, 40, 0, 600, 129, 255], 200),   # block size 8
     (8, 64, 8, 128, 32, torch.bfloat16, [16, 0, 400, 31, 1000, 7, 65, 300], 96),  # G = 8, bs 32
+    # head_dim 80 / 96 (padded to 128 tiles), on the multi-query kernels
+    (10, 32, 8, 80, 16, torch.bfloat16, [0, 50, 300, 1000, 17, 0, 2000, 64, 5, 700], 256),
+    (12, 14, 2, 96, 16, torch.float16, [1, 2, 3, 900, 100, 0, 33, 64, 65, 500, 8, 1200], 640),
 ]
 
 

@@ -14,6 +14,11 @@
 so the reference's scheduler, BlockPagedBatchCache.update, prefix cache and
 CUDA-graph decode manager run unchanged on top.  ``uninstall()`` restores the
 originals.  Nothing is imported from the reference unless ``install`` is called.
+
+Inputs on the CPU (a query tensor, or a pool, that is not on a CUDA device) keep
+the reference's own function: the sm_100a kernels serve CUDA tensors, and the
+reference's CPU path is its own code, not a stand-in for them.  CUDA inputs only
+ever reach the kernels, which fail loudly when the library is missing.
 """
 
 from __future__ import annotations
@@ -38,14 +43,28 @@ PATCH_POINTS = (
 _saved: dict[tuple[str, str], object] = {}
 
 
-def _replacement(module: str, name: str):
+def _replacement(module: str, name: str, original):
     if name == "GpuKVBlockPool.write_tokens_batch":
         def write_tokens_batch(self, layer_idx, block_tables, start_positions, key_states, value_states):
+            if self.device.type != "cuda":
+                return original(self, layer_idx, block_tables, start_positions, key_states, value_states)
             write_tokens_batch_into(self, layer_idx, block_tables, start_positions, key_states, value_states)
 
         write_tokens_batch.__doc__ = write_tokens_batch_into.__doc__
         return write_tokens_batch
-    return getattr(reference_api, name)
+    ours = getattr(reference_api, name)
+    if name == "triton_available":
+        return ours
+
+    def by_device(*args, **kwargs):
+        query = kwargs.get("query", args[0] if args else None)
+        if query is not None and not query.is_cuda:
+            return original(*args, **kwargs)
+        return ours(*args, **kwargs)
+
+    by_device.__name__, by_device.__doc__ = ours.__name__, ours.__doc__
+    by_device.b200_impl = ours
+    return by_device
 
 
 def _resolve(mod: ModuleType, dotted: str):
@@ -65,7 +84,7 @@ def install() -> list[str]:
         key = (module_name, dotted)
         if key not in _saved:
             _saved[key] = getattr(owner, attr)
-        setattr(owner, attr, _replacement(module_name, dotted))
+        setattr(owner, attr, _replacement(module_name, dotted, _saved[key]))
         done.append(f"{module_name}.{dotted}")
     return done
 

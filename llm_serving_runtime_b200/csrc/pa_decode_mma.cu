@@ -473,24 +473,31 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       const int rows_here = min(16, p.GQ - mg * 16);
       const bool r0_ok = qrow0 < rows_here;
       const bool r1_ok = qrow0 + 8 < rows_here;
-      if (row_end && piece_from_row_start) {
-        // The whole row is in this piece: normalise and store.
+      // Normalise and store this thread's two rows of the row group from a
+      // complete (m, l, acc) state in the MMA fragment layout: to every
+      // destination under the fused gather, after folding the prefix state in
+      // under the cascade.
+      auto finalize_rows = [&](float mm0, float mm1, float ll0, float ll1) {
         const int qa0 = mg * 16 + qrow0, qa1 = qa0 + 8;
         T* op0 = r0_ok ? out_row(0, b, h * p.G + qa0 % p.G, qa0 / p.G) : nullptr;
         T* op1 = r1_ok ? out_row(0, b, h * p.G + qa1 % p.G, qa1 / p.G) : nullptr;
         if constexpr (gather) {
           for (int dst = 0; dst < n_dst; ++dst)
             store_rows<T, D>(r0_ok ? out_row(dst, b, h * p.G + qa0 % p.G, qa0 / p.G) : nullptr,
-                             r1_ok ? out_row(dst, b, h * p.G + qa1 % p.G, qa1 / p.G) : nullptr, o_acc, lt0, lt1,
+                             r1_ok ? out_row(dst, b, h * p.G + qa1 % p.G, qa1 / p.G) : nullptr, o_acc, ll0, ll1,
                              quad, p.Dv);
         } else if (cascade && s_u0[b] > 0) {
           const long long rb = (long long)b * p.Hq + h * p.G;
           const long long ridx0 = (rb + qa0 % p.G) * p.q_len + qa0 / p.G;
           const long long ridx1 = (rb + qa1 % p.G) * p.q_len + qa1 / p.G;
-          store_rows_folded<T, D>(op0, op1, o_acc, m0, m1, lt0, lt1, ridx0, ridx1, p, quad);
+          store_rows_folded<T, D>(op0, op1, o_acc, mm0, mm1, ll0, ll1, ridx0, ridx1, p, quad);
         } else {
-          store_rows<T, D>(op0, op1, o_acc, lt0, lt1, quad, p.Dv);
+          store_rows<T, D>(op0, op1, o_acc, ll0, ll1, quad, p.Dv);
         }
+      };
+      if (row_end && piece_from_row_start) {
+        // The whole row is in this piece: normalise and store.
+        finalize_rows(m0, m1, lt0, lt1);
       } else {
         // Partial: (m, l, acc) to this warp's slot, then count the arrival.
         const int slot_idx = 2 * gw + (piece_first ? 0 : 1);
@@ -530,10 +537,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         if (lane == 0) old = atomicAdd(&p.counters[row_id], 1);
         old = __shfl_sync(0xffffffffu, old, 0);
         if (old == npieces - 1) {
-          // Last arrival: log-sum-exp merge of all pieces of this row.  Lanes
-          // span the pieces for the max and the weights; each piece's partial
-          // accumulators are then read for 8 rows at a time, all loads of a
-          // piece in flight together.
+          // Last arrival: log-sum-exp merge of all pieces of this row.
           __threadfence();
           const bool gw1_first = (W * gw1 / nw_eff) == row_start;
           auto slot_ptr = [&](int i) -> const float* {
@@ -541,6 +545,63 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
             const int si = (i == 0 && !gw1_first) ? 2 * g2 + 1 : 2 * g2;
             return p.partials + (long long)si * slot_floats;
           };
+          if (npieces <= kFragMergePieces) {
+            // Few pieces: merge in the MMA fragment layout (each thread its two
+            // rows' columns), every piece's loads in flight together, in piece
+            // order -- the result does not depend on which warp merges.  The
+            // merged state then goes out like a whole row.
+            float pm0[kFragMergePieces], pm1[kFragMergePieces], pl0[kFragMergePieces], pl1[kFragMergePieces];
+            float M0 = -INFINITY, M1 = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < kFragMergePieces; ++i) {
+              pm0[i] = pm1[i] = -INFINITY;
+              pl0[i] = pl1[i] = 0.f;
+              if (i < npieces) {
+                const float* ps = slot_ptr(i);
+                if (r0_ok) {
+                  pm0[i] = __ldcg(ps + qrow0);
+                  pl0[i] = __ldcg(ps + p.slot_rows + qrow0);
+                }
+                if (r1_ok) {
+                  pm1[i] = __ldcg(ps + qrow0 + 8);
+                  pl1[i] = __ldcg(ps + p.slot_rows + qrow0 + 8);
+                }
+              }
+              M0 = fmaxf(M0, pm0[i]);
+              M1 = fmaxf(M1, pm1[i]);
+            }
+            const float base0 = (M0 == -INFINITY) ? 0.f : M0;
+            const float base1 = (M1 == -INFINITY) ? 0.f : M1;
+            float L0 = 0.f, L1 = 0.f;
+#pragma unroll
+            for (int nd = 0; nd < NDT; ++nd) o_acc[nd][0] = o_acc[nd][1] = o_acc[nd][2] = o_acc[nd][3] = 0.f;
+#pragma unroll
+            for (int i = 0; i < kFragMergePieces; ++i) {
+              if (i < npieces) {
+                const float w0 = ex2(pm0[i] - base0), w1 = ex2(pm1[i] - base1);
+                L0 = fmaf(w0, pl0[i], L0);
+                L1 = fmaf(w1, pl1[i], L1);
+                const float* so = slot_ptr(i) + 2 * p.slot_rows;
+#pragma unroll
+                for (int nd = 0; nd < NDT; ++nd) {
+                  const int d = nd * 8 + 2 * quad;
+                  const float2 a0 = r0_ok ? __ldcg(reinterpret_cast<const float2*>(so + qrow0 * D + d))
+                                          : make_float2(0.f, 0.f);
+                  const float2 a1 = r1_ok ? __ldcg(reinterpret_cast<const float2*>(so + (qrow0 + 8) * D + d))
+                                          : make_float2(0.f, 0.f);
+                  o_acc[nd][0] = fmaf(w0, a0.x, o_acc[nd][0]);
+                  o_acc[nd][1] = fmaf(w0, a0.y, o_acc[nd][1]);
+                  o_acc[nd][2] = fmaf(w1, a1.x, o_acc[nd][2]);
+                  o_acc[nd][3] = fmaf(w1, a1.y, o_acc[nd][3]);
+                }
+              }
+            }
+            finalize_rows(M0, M1, L0, L1);
+            if (lane == 0) atomicExch(&p.counters[row_id], 0);
+          } else {
+          // Many pieces: lanes span the pieces for the max and the weights;
+          // each piece's partial accumulators are then read for a few rows at
+          // a time, all loads of a piece in flight together.
           constexpr int RG = DPL >= 4 ? 4 : 8;  // rows merged per pass (register budget)
           for (int rg = 0; rg < rows_here; rg += RG) {
             float M[RG], lsum[RG], acc[RG][DPL];
@@ -626,6 +687,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
             }
           }
           if (lane == 0) atomicExch(&p.counters[row_id], 0);
+          }
         }
       }
     }

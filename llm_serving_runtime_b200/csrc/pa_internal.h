@@ -24,6 +24,9 @@ constexpr int kUmmaThreads = 10 * 32;
 // Minimum number of 16-token units a warp's share of the flat work list holds
 // before the kernel stops splitting the work further.
 constexpr int kMinUnitsPerWarp = 8;
+// Split rows of at most this many pieces are merged in the MMA fragment layout
+// (all loads in flight at once); longer ones by the lane-parallel merge.
+constexpr int kFragMergePieces = 4;
 // Layout of the workspace: status word, then merge counters, then partial slots.
 constexpr size_t kWsHeaderBytes = 256;
 

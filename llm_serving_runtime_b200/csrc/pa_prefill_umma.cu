@@ -23,8 +23,8 @@
 //
 // While one tile's softmax runs, the tensor core works on the other tile's
 // products, so neither waits for the other.  Each tile has two S/P buffers in
-// TMEM; the MMA thread refills a buffer only after the PV that read its P has
-// completed.  The online softmax keeps a reference max per row and rescales O
+// TMEM; the MMA thread refills a buffer right after issuing the PV that reads
+// its P (the tensor core runs one thread's MMAs in issue order).  The online softmax keeps a reference max per row and rescales O
 // (TMEM load, scale, store) only when a chunk raises the row max by more than
 // 2^8, so p stays below 256 and the arithmetic is exact; most chunks skip the
 // rescale.  Every wait is bounded; TMEM is always released before the CTA exits.
@@ -348,26 +348,29 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       bool ok = mbar_wait_bounded(smem_addr(q_ready), 0);
       const uint32_t id_s = umma_idesc(128, kChunk, FMT, 0);
       const uint32_t id_o = umma_idesc(128, D, FMT, 1);
+      // Descriptors built once per buffer; a k-step only advances the start
+      // address field (addresses stay below 256 KB: no carry out of it).
+      const uint64_t qdesc[2] = {umma_desc(smem_addr(s_q), 16, 1024), umma_desc(smem_addr(s_q + QT_BYTES), 16, 1024)};
+      const uint64_t kdesc0 = umma_desc(smem_addr(s_kv), 16, 1024);
+      const uint64_t vdesc0 = umma_desc(smem_addr(s_kv) + HALVES * HALF_BYTES, HALF_BYTES, 1024);
       auto issue_qk = [&](int t, int jq) {
-        const uint32_t q_base = smem_addr(s_q + t * QT_BYTES);
-        const uint32_t k_base = smem_addr(s_kv + (jq % S) * KV_BYTES);
+        const uint64_t kd = kdesc0 + (uint64_t)(((jq % S) * KV_BYTES) >> 4);
         const uint32_t d = tmem + (uint32_t)(t * 256 + (jq & 1) * kChunk);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t hoff = (uint32_t)(ks >> 2);
-          const uint32_t koff = (uint32_t)(ks & 3) * 32u;
-          umma_f16(d, umma_desc(q_base + hoff * 16384u + koff, 16, 1024),
-                   umma_desc(k_base + hoff * HALF_BYTES + koff, 16, 1024), id_s, ks > 0 ? 1u : 0u);
+          const uint64_t step_q = (uint64_t)(((ks >> 2) * 16384u + (ks & 3) * 32u) >> 4);
+          const uint64_t step_k = (uint64_t)(((ks >> 2) * HALF_BYTES + (ks & 3) * 32u) >> 4);
+          umma_f16(d, qdesc[t] + step_q, kd + step_k, id_s, ks > 0 ? 1u : 0u);
         }
         umma_commit(smem_addr(&s_full[t * 2 + (jq & 1)]));
       };
       auto issue_pv = [&](int t, int jp) {
-        const uint32_t v_base = smem_addr(s_kv + (jp % S) * KV_BYTES) + HALVES * HALF_BYTES;
+        const uint64_t vb = vdesc0 + (uint64_t)(((jp % S) * KV_BYTES) >> 4);
         const uint32_t pcol = tmem + (uint32_t)(t * 256 + (jp & 1) * kChunk);  // P hi: +0..31, lo: +32..63
         const uint32_t o = tmem + (uint32_t)(t * 256 + 128);
 #pragma unroll
         for (int ks = 0; ks < kChunk / 16; ++ks) {
-          const uint64_t vd = umma_desc(v_base + ks * 2048u, HALF_BYTES, 1024);
+          const uint64_t vd = vb + (uint64_t)((ks * 2048u) >> 4);
           umma_f16_tmem_a(o, pcol + ks * 8u, vd, id_o, (jp > 0 || ks > 0) ? 1u : 0u);
           if (kSplit) umma_f16_tmem_a(o, pcol + 32u + ks * 8u, vd, id_o, 1u);
         }
@@ -385,12 +388,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         if (jn < n_chunks) {
           ok = mbar_wait_bounded(smem_addr(&kv_full[jn % S]), (uint32_t)((jn / S) & 1));
           for (int t = 0; t < ntiles && ok; ++t) {
-            // the buffer's previous P (chunk jn - 2) must have been consumed
-            if (jn >= 2) ok = mbar_wait_bounded(smem_addr(&pv_done[t * 2 + (jn & 1)]), (uint32_t)(((jn - 2) >> 1) & 1));
-            if (ok) {
-              tmem_fence_after();
-              issue_qk(t, jn);
-            }
+            // The buffer's previous P (chunk jn - 2) is read by a P.V this
+            // thread issued before; tcgen05.mma operations of one thread run
+            // in issue order, so S of chunk jn can go into it at once.
+            tmem_fence_after();
+            issue_qk(t, jn);
           }
           if (!ok) break;
         }

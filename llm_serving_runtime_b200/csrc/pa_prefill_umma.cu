@@ -136,6 +136,19 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Two probabilities (>= 0) as packed bf16 pairs hi and lo with p ~ hi + lo,
+// both by truncation with bit operations: hi keeps the upper 16 bits of p, lo
+// those of the exact fp32 residual p - hi.  hi + lo carries about 15 bits of p
+// (relative error below 2^-15) and, unlike round-to-nearest conversions, takes
+// no conversion instructions, which share the exp2 unit's throughput.
+__device__ __forceinline__ void split_bf16_pair(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+  const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
+  hi = __byte_perm(b0, b1, 0x7632);  // low half: p0's upper 16 bits; high half: p1's
+  const float r0 = p0 - __uint_as_float(b0 & 0xffff0000u);
+  const float r1 = p1 - __uint_as_float(b1 & 0xffff0000u);
+  lo = __byte_perm(__float_as_uint(r0), __float_as_uint(r1), 0x7632);
+}
+
 // Byte offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled region.
 __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
@@ -213,10 +226,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     }
     n_chunks = (row0 < rows_total && kv_end > kv_lo) ? (kv_end - kv_lo + kChunk - 1) / kChunk : 0;
   } else {
-    const int BH = p.B * p.Hkv;
     const int MT = (p.GQ + kTileRows - 1) / kTileRows;
-    const int mt = MT - 1 - (int)(blockIdx.x / BH);  // latest (heaviest) row blocks first
-    const int bh = (int)(blockIdx.x % BH);
+    // The CTAs of one (sequence, kv head) read the same K/V: adjacent block
+    // indices put them in the same wave, so all but the first read hit L2.
+    // Within a (sequence, kv head), the latest (heaviest) row blocks first.
+    const int mt = MT - 1 - (int)(blockIdx.x % MT);
+    const int bh = (int)(blockIdx.x / MT);
     b_kv = bh / p.Hkv;
     h = bh - b_kv * p.Hkv;
     int L = p.context_lens[b_kv] + p.len_offset;
@@ -287,57 +302,52 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       const int chunk0 = kv_lo + j * kChunk;
       // units of this chunk the token range reaches
       const int units = min(4, (kv_end - chunk0 + 15) / 16);
-      uint32_t tx = 0;
-      int physs[4][2];
-      for (int u = 0; u < 4; ++u) {
-        const int tok0 = chunk0 + u * 16;
-        const int lb0 = tok0 / bs;
-        const int need = bs >= 16 ? 1 : 16 / bs;
-        if (win_base < 0 || lb0 < win_base || lb0 + need > win_base + 32) {
-          win_base = lb0;
-          const int e = lb0 + lane;
+      // block-table window (32 entries, one per lane) covering every block of the chunk
+      {
+        const int lb_first = chunk0 / bs, lb_last = (chunk0 + kChunk - 1) / bs;
+        if (win_base < 0 || lb_first < win_base || lb_last >= win_base + 32) {
+          win_base = lb_first;
+          const int e = lb_first + lane;
           win_val = (e < p.max_blocks) ? __ldg(&p.block_tables[(long long)b_kv * p.bt_stride + e]) : -1;
         }
-        physs[u][0] = __shfl_sync(0xffffffffu, win_val, lb0 - win_base);
-        physs[u][1] = __shfl_sync(0xffffffffu, win_val, (lb0 + 1 - win_base) & 31);
       }
+      // Lane -> (unit, K or V, 64-column half): every box of the chunk is issued
+      // by its own lane in one instruction.  A single thread issuing them one
+      // after another keeps only about one chunk in flight.
+      const int u = lane / (2 * HALVES);
+      const int is_v = (lane / HALVES) & 1;
+      const int hf = lane % HALVES;
+      const int tok0 = chunk0 + u * 16;
+      const int lb0 = tok0 / bs;
+      const int ph0 = __shfl_sync(0xffffffffu, win_val, (lb0 - win_base) & 31);
+      const int ph1 = __shfl_sync(0xffffffffu, win_val, (lb0 + 1 - win_base) & 31);
       if (lane == 0) {
-        for (int u = 0; u < units; ++u) {
-          const int tok0 = chunk0 + u * 16;
+        uint32_t tx = 0;
+        for (int v = 0; v < units; ++v) {
+          const int t0 = chunk0 + v * 16;
           if (bs >= 16) {
             tx += 2u * HALVES * 2048u;
           } else {
-            const bool need1 = (tok0 / bs + 1) * bs < kv_end;
+            const bool need1 = (t0 / bs + 1) * bs < kv_end;
             tx += (need1 ? 2u : 1u) * 2u * HALVES * (uint32_t)bs * 128u;
           }
         }
         mbar_arrive_expect_tx(bar, tx);
-        for (int u = 0; u < units; ++u) {
-          const int tok0 = chunk0 + u * 16;
-          const int lb0 = tok0 / bs;
-          if (bs >= 16) {
-            const int phys = physs[u][0];
-            const int y = tok0 - lb0 * bs;
-            if (phys < 0 || phys >= p.num_blocks) raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
-#pragma unroll
-            for (int hf = 0; hf < HALVES; ++hf) {
-              tma_load_4d(base + hf * HALF_BYTES + u * 2048u, &tmk, bar, hf * 64, y, h, phys);
-              tma_load_4d(base + (HALVES + hf) * HALF_BYTES + u * 2048u, &tmv, bar, hf * 64, y, h, phys);
-            }
-          } else {
-            const bool need1 = (lb0 + 1) * bs < kv_end;
-            const uint32_t box = (uint32_t)bs * 128u;
-            for (int jj = 0; jj < (need1 ? 2 : 1); ++jj) {
-              const int phys = physs[u][jj];
-              if (phys < 0 || phys >= p.num_blocks) raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
-#pragma unroll
-              for (int hf = 0; hf < HALVES; ++hf) {
-                tma_load_4d(base + hf * HALF_BYTES + u * 2048u + jj * box, &tmk, bar, hf * 64, 0, h, phys);
-                tma_load_4d(base + (HALVES + hf) * HALF_BYTES + u * 2048u + jj * box, &tmv, bar, hf * 64, 0, h,
-                            phys);
-              }
-            }
-          }
+      }
+      __syncwarp();
+      if (u < units) {
+        const CUtensorMap* map = is_v ? &tmv : &tmk;
+        const uint32_t dst = base + (uint32_t)(is_v * HALVES + hf) * HALF_BYTES + (uint32_t)u * 2048u;
+        const bool check = !is_v && hf == 0;
+        if (bs >= 16) {
+          if (check && (ph0 < 0 || ph0 >= p.num_blocks)) raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
+          tma_load_4d(dst, map, bar, hf * 64, tok0 - lb0 * bs, h, ph0);
+        } else {
+          const bool need1 = (lb0 + 1) * bs < kv_end;
+          if (check && (ph0 < 0 || ph0 >= p.num_blocks || (need1 && (ph1 < 0 || ph1 >= p.num_blocks))))
+            raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
+          tma_load_4d(dst, map, bar, hf * 64, 0, h, ph0);
+          if (need1) tma_load_4d(dst + (uint32_t)bs * 128u, map, bar, hf * 64, 0, h, ph1);
         }
       }
       __syncwarp();
@@ -544,8 +554,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           const float p0 = ex2(fmaf(x[16 * piece + 2 * i], sl2, nbase));
           const float p1 = ex2(fmaf(x[16 * piece + 2 * i + 1], sl2, nbase));
           ps += p0 + p1;
-          hi[i] = pack2<T>(p0, p1);
-          lo[i] = kSplit ? pack2<T>(p0 - lo_half<T>(hi[i]), p1 - hi_half<T>(hi[i])) : 0u;
+          if constexpr (kSplit) {
+            split_bf16_pair(p0, p1, hi[i], lo[i]);
+          } else {
+            hi[i] = pack2<T>(p0, p1);
+            lo[i] = 0u;
+          }
         }
         tmem_st8(t_s + sb * kChunk + piece * 8, hi);
         if (kSplit) tmem_st8(t_s + sb * kChunk + 32 + piece * 8, lo);

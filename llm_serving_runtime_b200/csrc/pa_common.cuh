@@ -188,6 +188,10 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
   return v;
 }
+// Bring the 128-byte line holding `ptr` into L2 (no register result).
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
 // Nanoseconds of the GPU's global timer.
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;

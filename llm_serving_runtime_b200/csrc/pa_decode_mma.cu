@@ -324,8 +324,27 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     }
   };
 
+  // Cascade: when the last unit of a row group is issued, pull the group's
+  // prefix state (m, l and the unnormalised accumulator, which the prefix
+  // kernel left) into L2, so the fold at the row end does not wait on HBM.
+  // Lane pairs take one row each, a half-row of the accumulator per lane.
+  auto prefetch_prefix_state = [&](int b, int h, int mg) {
+    const int qr = mg * 16 + (lane >> 1);
+    if (qr < p.GQ) {
+      const int t = qr / p.G, g = qr - t * p.G;
+      const long long ridx = ((long long)b * p.Hq + h * p.G + g) * p.q_len + t;
+      const float* a = p.pre_acc + ridx * D + (lane & 1) * (D / 2);
+#pragma unroll
+      for (int c = 0; c < D / 2; c += 32) prefetch_l2(a + c);
+      if ((lane & 1) == 0) prefetch_l2(&p.pre_ml[ridx]);
+    }
+  };
+
   auto issue = [&](int slot) {
     const int h = pc.h;
+    if constexpr (cascade) {
+      if (pc.u + 1 == pc.n) prefetch_prefix_state(pc.b, h, pc.mg);
+    }
     const uint32_t stage = my_ring + (uint32_t)slot * STAGE_BYTES;
     const uint32_t bar = my_bars + (uint32_t)slot * 8u;
     const int tok0 = (pc.u + (cascade ? s_u0[pc.b] : 0)) * kUnitTokens;

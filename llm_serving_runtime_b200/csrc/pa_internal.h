@@ -19,8 +19,9 @@ constexpr int kPrefillWarps = 8;
 constexpr int kPrefillThreads = (kPrefillWarps + 1) * 32;
 constexpr int kPrefillStages = 6;
 // tcgen05 multi-query kernel: 2 x 4 softmax warps (two 128-row tiles) + 1 TMA
-// producer + 1 MMA-issue warp.
-constexpr int kUmmaThreads = 10 * 32;
+// producer + 1 MMA-issue warp; the cascade's prefix pass adds a warp for its
+// member table check (11 warps keep the 168-register budget that 10 have).
+constexpr int umma_threads(bool prefix) { return (prefix ? 11 : 10) * 32; }
 // Minimum number of 16-token units a warp's share of the flat work list holds
 // before the kernel stops splitting the work further.
 constexpr int kMinUnitsPerWarp = 8;

@@ -161,7 +161,7 @@ __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) { return (uint32_t
 // group's shared blocks in the split's token range through the first member's
 // block table, and leaves (m, l, unnormalised O) per row.
 template <typename T, int D, bool kPrefix>
-__global__ void __launch_bounds__(kUmmaThreads, 1)
+__global__ void __launch_bounds__(umma_threads(kPrefix), 1)
     prefill_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                         const DecodeParams p) {
   constexpr int HALVES = D / 64;
@@ -400,8 +400,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           for (int t = 0; t < ntiles && ok; ++t) {
             // The buffer's previous P (chunk jn - 2) is read by a P.V this
             // thread issued before; tcgen05.mma operations of one thread run
-            // in issue order, so S of chunk jn can go into it at once.
-            tmem_fence_after();
+            // in issue order, so S of chunk jn can go into it at once.  No
+            // tcgen05 fence here (one costs ~100 cycles of this thread's
+            // issue): the softmax's reads of that buffer were ordered before
+            // this thread's MMAs by the fence after the P wait of that P.V,
+            // and K is ordered by its full barrier like any TMA-fed operand.
             issue_qk(t, jn);
           }
           if (!ok) break;
@@ -417,30 +420,41 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         umma_commit(smem_addr(&kv_empty[j % S]));
       }
       if (!ok) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
-    } else if constexpr (kPrefix) {
-      // Idle lanes: every member must reach the shared prefix through the same
-      // physical blocks as the first member (whose table the producer reads).
-      // Checked once per member, by the split-0 / head-0 CTA holding its first row.
-      if (lane > 0 && split == 0 && h == 0 && prefix_tokens > 0) {
-        const int i_lo = (row0 + p.GQ - 1) / p.GQ;
-        const int i_hi = min(rows_total, row0 + kTileRows);  // rows; members i with i*GQ < i_hi
-        const int nblk = (prefix_tokens + p.bs - 1) / p.bs;
-        bool bad = false;
-        for (int i = i_lo; i * p.GQ < i_hi; ++i) {
-          const int bm = p.member_seq[moff + i];
-          if (bm == b_kv) continue;
-          if (bm < 0 || bm >= p.B) {
-            bad = true;
-            continue;
-          }
-          for (int k = lane - 1; k < nblk; k += 31)
-            bad |= __ldg(&p.block_tables[(long long)bm * p.bt_stride + k]) !=
-                   __ldg(&p.block_tables[(long long)b_kv * p.bt_stride + k]);
-        }
-        if (bad) raise_flag(p.status, PA_DEVERR_PREFIX);
-      }
     }
     __syncwarp();
+  } else if (warp == 10) {
+    // ---------------- prefix pass: member table check ----------------
+    // Every member must reach the shared prefix through the same physical
+    // blocks as the first member, whose table the producer reads.  The
+    // split-0 / head-0 CTA holding a member's first row checks it, in this
+    // warp of its own so the loads overlap the pipeline.  Member ids come 32 at
+    // a time and every table load of a pass is independent.
+    if constexpr (kPrefix) {
+      if (split == 0 && h == 0 && prefix_tokens > 0 && row0 < rows_total) {
+        const int i_lo = (row0 + p.GQ - 1) / p.GQ;
+        const int i_end = (min(rows_total, row0 + kTileRows) + p.GQ - 1) / p.GQ;  // members i_lo .. i_end - 1
+        const int nblk = (prefix_tokens + p.bs - 1) / p.bs;
+        const int* first = p.block_tables + (long long)b_kv * p.bt_stride;
+        bool bad = false;
+        for (int m0 = i_lo; m0 < i_end; m0 += 32) {
+          const int my_member = m0 + lane < i_end ? p.member_seq[moff + m0 + lane] : b_kv;
+          const int nm = min(32, i_end - m0);
+          for (int k0 = 0; k0 < nblk; k0 += 32) {
+            const int k = k0 + lane;
+            const bool kin = k < nblk;
+            const int f = kin ? __ldg(first + k) : 0;
+#pragma unroll 8
+            for (int jm = 0; jm < nm; ++jm) {
+              const int bm = __shfl_sync(0xffffffffu, my_member, jm);
+              const bool valid = bm >= 0 && bm < p.B;
+              const int e = (kin && valid && bm != b_kv) ? __ldg(p.block_tables + (long long)bm * p.bt_stride + k) : f;
+              bad |= !valid || e != f;
+            }
+          }
+        }
+        if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(p.status, PA_DEVERR_PREFIX);
+      }
+    }
   } else {
     // ---------------- softmax warps: tile t, thread = query row = TMEM lane ----------------
     const int t = warp >> 2;             // MMA tile of this warpgroup
@@ -725,7 +739,7 @@ static cudaError_t launch_umma_impl(const DecodeParams& p, const CUtensorMap& tm
               : (long long)p.B * p.Hkv * ((p.GQ + kTileRows - 1) / kTileRows);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ctas);
-  cfg.blockDim = dim3(kUmmaThreads);
+  cfg.blockDim = dim3(umma_threads(kPrefix));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

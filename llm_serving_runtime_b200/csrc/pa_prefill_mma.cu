@@ -37,10 +37,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int BH = p.B * p.Hkv;
   const int MT = (p.GQ + 127) / 128;
-  const int mt = MT - 1 - (int)(blockIdx.x / BH);  // latest (heaviest) tiles first
-  const int bh = (int)(blockIdx.x % BH);
+  // The tiles of one (sequence, kv head) read the same K/V: adjacent block
+  // indices run them in the same wave, so all but the first read hit L2.
+  // Within a (sequence, kv head), the latest (heaviest) tiles first.
+  const int mt = MT - 1 - (int)(blockIdx.x % MT);
+  const int bh = (int)(blockIdx.x / MT);
   const int b = bh / p.Hkv;
   const int h = bh - b * p.Hkv;
 
@@ -95,33 +97,24 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
       const int phys0 = __shfl_sync(0xffffffffu, win_val, lb0 - win_base);
       const int phys1 = __shfl_sync(0xffffffffu, win_val, (lb0 + 1 - win_base) & 31);
+      // One box per lane (K or V x 64-column half, x block for size 8), in one
+      // instruction: a thread's bulk-tensor copies issue one after another.
+      const uint32_t stage = ring + (uint32_t)slot * STAGE_BYTES;
+      const uint32_t bar = smem_addr(&full[slot]);
+      const bool need1 = bs < kUnitTokens && (lb0 + 1) * bs < L;
+      const uint32_t box_bytes = bs >= kUnitTokens ? 2048u : (uint32_t)bs * 128u;
+      const int nbox = (need1 ? 2 : 1) * HALVES * 2;
       if (lane == 0) {
-        const uint32_t stage = ring + (uint32_t)slot * STAGE_BYTES;
-        const uint32_t bar = smem_addr(&full[slot]);
-        if (bs >= kUnitTokens) {
-          const int y = tok0 - lb0 * bs;
-          if (phys0 < 0 || phys0 >= p.num_blocks) raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
-          mbar_arrive_expect_tx(bar, STAGE_BYTES);
-#pragma unroll
-          for (int hf = 0; hf < HALVES; ++hf) {
-            tma_load_4d(stage + hf * 2048u, &tmk, bar, hf * 64, y, h, phys0);
-            tma_load_4d(stage + TILE_BYTES + hf * 2048u, &tmv, bar, hf * 64, y, h, phys0);
-          }
-        } else {  // block size 8: two blocks per unit, the second only if the sequence reaches it
-          const bool need1 = (lb0 + 1) * bs < L;
-          const uint32_t box_bytes = (uint32_t)bs * 128u;
-          if (phys0 < 0 || phys0 >= p.num_blocks || (need1 && (phys1 < 0 || phys1 >= p.num_blocks)))
-            raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
-          mbar_arrive_expect_tx(bar, (need1 ? 2u : 1u) * HALVES * 2u * box_bytes);
-          for (int j = 0; j < (need1 ? 2 : 1); ++j) {
-            const int phys = j ? phys1 : phys0;
-#pragma unroll
-            for (int hf = 0; hf < HALVES; ++hf) {
-              tma_load_4d(stage + hf * 2048u + j * box_bytes, &tmk, bar, hf * 64, 0, h, phys);
-              tma_load_4d(stage + TILE_BYTES + hf * 2048u + j * box_bytes, &tmv, bar, hf * 64, 0, h, phys);
-            }
-          }
-        }
+        if (phys0 < 0 || phys0 >= p.num_blocks || (need1 && (phys1 < 0 || phys1 >= p.num_blocks)))
+          raise_flag(p.status, PA_DEVERR_BLOCK_ID_RANGE);
+        mbar_arrive_expect_tx(bar, (uint32_t)nbox * box_bytes);
+      }
+      __syncwarp();
+      if (lane < nbox) {  // lane -> (block j, K or V, half)
+        const int j = lane / (2 * HALVES), kv = (lane / HALVES) & 1, hf = lane % HALVES;
+        const int y = bs >= kUnitTokens ? tok0 - lb0 * bs : 0;
+        tma_load_4d(stage + (uint32_t)kv * TILE_BYTES + (uint32_t)hf * 2048u + (uint32_t)j * box_bytes,
+                    kv ? &tmv : &tmk, bar, hf * 64, y, h, j ? phys1 : phys0);
       }
       __syncwarp();
     }

@@ -56,3 +56,20 @@ def test_prefill_workload_with_append_sampled_rows():
     rows = [0, 5, 11]
     ref = oracle_rows(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale, w.q_len, rows)
     assert excess_err(out[rows], ref) <= 0, f"max abs err {max_err(out[rows], ref)}"
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,bs,dtype,lens,q_len", CASES[8:12])
+def test_mma_multi_query_kernel_on_unaligned_output(B, Hq, Hkv, D, bs, dtype, lens, q_len):
+    """Output rows that are 4- but not 16-byte aligned take the mma.sync
+    multi-query kernel (the tcgen05 one stores whole 16-byte pieces); same
+    results."""
+    from llm_serving_runtime_b200 import _lib
+
+    q, kc, vc, bt, cl = _synthetic(B, Hq, Hkv, D, bs, dtype, lens, q_len, seed=q_len + D + 1)
+    buf = torch.full((B * Hq * q_len * D + 2,), float("nan"), dtype=dtype, device=DEV)
+    out = buf[2:].view(B, Hq, q_len, D)
+    paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), D ** -0.5, out=out,
+                           validate=True)
+    assert _lib.last_kernel() == "pa::prefill_mma_kernel"
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, D ** -0.5)
+    assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"

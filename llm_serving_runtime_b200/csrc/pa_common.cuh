@@ -63,6 +63,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for phase `parity` of an mbarrier.  Returns false on timeout.
+// Non-blocking probe of a phase (mbarrier.test_wait).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+
+// mbar_wait_bounded that first probes without blocking.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity);
+__device__ __forceinline__ bool mbar_test_then_wait(uint32_t bar, uint32_t parity) {
+  return mbar_test(bar, parity) || mbar_wait_bounded(bar, parity);
+}
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();

@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
 
     // ---- wait for this unit's K/V tiles ----
     const uint32_t bar = my_bars + (uint32_t)slot * 8u;
-    if (!mbar_wait_bounded(bar, (phase >> slot) & 1u)) {
+    if (!mbar_test_then_wait(bar, (phase >> slot) & 1u)) {
       if (lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
       // Drain this warp's copies still in flight (bounded), then leave.
       int s = slot;

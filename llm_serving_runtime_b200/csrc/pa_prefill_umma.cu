@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
       for (int j = 0; j < n_chunks && ok; ++j) {
         const int jn = j + 1;
         if (jn < n_chunks) {
-          ok = mbar_wait_bounded(smem_addr(&kv_full[jn % S]), (uint32_t)((jn / S) & 1));
+          ok = mbar_test_then_wait(smem_addr(&kv_full[jn % S]), (uint32_t)((jn / S) & 1));
           for (int t = 0; t < ntiles && ok; ++t) {
             // The buffer's previous P (chunk jn - 2) is read by a P.V this
             // thread issued before; tcgen05.mma operations of one thread run
@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
           if (!ok) break;
         }
         for (int t = 0; t < ntiles && ok; ++t) {
-          ok = mbar_wait_bounded(smem_addr(&p_full[t * 2 + (j & 1)]), (uint32_t)((j >> 1) & 1));
+          ok = mbar_test_then_wait(smem_addr(&p_full[t * 2 + (j & 1)]), (uint32_t)((j >> 1) & 1));
           if (ok) {
             tmem_fence_after();
             issue_pv(t, j);
@@ -502,7 +502,7 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
     bool ok = true;
     for (int j = 0; j < n_chunks && tile_on; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait_bounded(smem_addr(&s_full[t * 2 + sb]), (uint32_t)((j >> 1) & 1))) {
+      if (!mbar_test_then_wait(smem_addr(&s_full[t * 2 + sb]), (uint32_t)((j >> 1) & 1))) {
         ok = false;
         break;
       }

@@ -391,29 +391,35 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
       if (ok) ok = mbar_wait_bounded(smem_addr(&kv_full[0]), 0);
       if (ok) {
         tmem_fence_after();
-        for (int t = 0; t < ntiles; ++t) issue_qk(t, 0);
+        issue_qk(0, 0);
+        if (ntiles > 1) issue_qk(1, 0);
       }
       for (int j = 0; j < n_chunks && ok; ++j) {
         const int jn = j + 1;
         if (jn < n_chunks) {
           ok = mbar_test_then_wait(smem_addr(&kv_full[jn % S]), (uint32_t)((jn / S) & 1));
-          for (int t = 0; t < ntiles && ok; ++t) {
-            // The buffer's previous P (chunk jn - 2) is read by a P.V this
-            // thread issued before; tcgen05.mma operations of one thread run
-            // in issue order, so S of chunk jn can go into it at once.  No
-            // tcgen05 fence here (one costs ~100 cycles of this thread's
-            // issue): the softmax's reads of that buffer were ordered before
-            // this thread's MMAs by the fence after the P wait of that P.V,
-            // and K is ordered by its full barrier like any TMA-fed operand.
-            issue_qk(t, jn);
-          }
           if (!ok) break;
+          // The buffer's previous P (chunk jn - 2) is read by a P.V this
+          // thread issued before; tcgen05.mma operations of one thread run in
+          // issue order, so S of chunk jn can go into it at once.  No tcgen05
+          // fence here (one costs ~100 cycles of this thread's issue): the
+          // softmax's reads of that buffer were ordered before this thread's
+          // MMAs by the fence after the P wait of that P.V, and K is ordered
+          // by its full barrier like any TMA-fed operand.  The tile index is a
+          // literal in each call, so the descriptors are fixed at compile time.
+          issue_qk(0, jn);
+          if (ntiles > 1) issue_qk(1, jn);
         }
-        for (int t = 0; t < ntiles && ok; ++t) {
-          ok = mbar_test_then_wait(smem_addr(&p_full[t * 2 + (j & 1)]), (uint32_t)((j >> 1) & 1));
-          if (ok) {
-            tmem_fence_after();
-            issue_pv(t, j);
+        ok = mbar_test_then_wait(smem_addr(&p_full[j & 1]), (uint32_t)((j >> 1) & 1));
+        if (ok) {
+          tmem_fence_after();
+          issue_pv(0, j);
+          if (ntiles > 1) {
+            ok = mbar_test_then_wait(smem_addr(&p_full[2 + (j & 1)]), (uint32_t)((j >> 1) & 1));
+            if (ok) {
+              tmem_fence_after();
+              issue_pv(1, j);
+            }
           }
         }
         if (!ok) break;

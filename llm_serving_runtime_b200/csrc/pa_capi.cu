@@ -202,8 +202,9 @@ struct CascadeShape {
 CascadeShape cascade_shape(int num_sms, int num_groups, int max_members, int max_prefix, int Hkv, int GQ,
                            long long rows, int D) {
   CascadeShape c;
-  // prefix-pass CTAs per split: 256 member rows each
-  const long long tiles = (long long)num_groups * Hkv * (((long long)max_members * GQ + 255) / 256);
+  // prefix-pass CTAs per split: kUmmaTileRows member rows each
+  const long long tiles =
+      (long long)num_groups * Hkv * (((long long)max_members * GQ + pa::kUmmaTileRows - 1) / pa::kUmmaTileRows);
   const int chunk = pa::kUmmaChunkTokens;
   const int prefix = max_prefix > 0 ? max_prefix : 0;
   int splits = 1;

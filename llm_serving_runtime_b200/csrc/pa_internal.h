@@ -130,6 +130,9 @@ cudaError_t launch_prefix_umma(const DecodeParams& p, const CUtensorMap& tmk, co
                                bool pdl, cudaStream_t stream);
 // Tokens per chunk of the tcgen05 kernels (prefix split ranges are multiples of it).
 constexpr int kUmmaChunkTokens = 64;
+// Query rows per CTA of the tcgen05 kernels (the prefix pass sizes its split
+// counters by it).
+constexpr int kUmmaTileRows = 256;
 
 // Shared-memory bytes of the tensor-core kernel for given stage count.
 size_t decode_mma_smem_bytes(int D, int B, int stages, bool cascade);

@@ -40,7 +40,7 @@ namespace {
 
 constexpr int kChunk = kUmmaChunkTokens;  // tokens per chunk (N of the QK^T MMA)
 constexpr uint32_t kTmemCols = 512;        // per tile: S/P buffers (2 x 64) + O (<= 128), at column 256 * tile
-constexpr int kTileRows = 256;             // query rows per CTA (two 128-row MMA tiles)
+constexpr int kTileRows = kUmmaTileRows;   // query rows per CTA (two 128-row MMA tiles)
 constexpr float kRescaleThreshold = 8.f;   // log2 units: rescale when the max grows by > 2^8
 
 // K/V chunks in flight: as many as the shared memory left after Q allows.

@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
       const uint64_t qdesc[2] = {umma_desc(smem_addr(s_q), 16, 1024), umma_desc(smem_addr(s_q + QT_BYTES), 16, 1024)};
       const uint64_t kdesc0 = umma_desc(smem_addr(s_kv), 16, 1024);
       const uint64_t vdesc0 = umma_desc(smem_addr(s_kv) + HALVES * HALF_BYTES, HALF_BYTES, 1024);
-      auto issue_qk = [&](int t, int jq) {
+      auto qk_mmas = [&](int t, int jq) {  // S_t(jq) = Q_t K(jq)^T
         const uint64_t kd = kdesc0 + (uint64_t)(((jq % S) * KV_BYTES) >> 4);
         const uint32_t d = tmem + (uint32_t)(t * 256 + (jq & 1) * kChunk);
 #pragma unroll
@@ -372,9 +372,8 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
           const uint64_t step_k = (uint64_t)(((ks >> 2) * HALF_BYTES + (ks & 3) * 32u) >> 4);
           umma_f16(d, qdesc[t] + step_q, kd + step_k, id_s, ks > 0 ? 1u : 0u);
         }
-        umma_commit(smem_addr(&s_full[t * 2 + (jq & 1)]));
       };
-      auto issue_pv = [&](int t, int jp) {
+      auto pv_mmas = [&](int t, int jp) {  // O_t += P_t(jp) V(jp)
         const uint64_t vb = vdesc0 + (uint64_t)(((jp % S) * KV_BYTES) >> 4);
         const uint32_t pcol = tmem + (uint32_t)(t * 256 + (jp & 1) * kChunk);  // P hi: +0..31, lo: +32..63
         const uint32_t o = tmem + (uint32_t)(t * 256 + 128);
@@ -384,20 +383,34 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
           umma_f16_tmem_a(o, pcol + ks * 8u, vd, id_o, (jp > 0 || ks > 0) ? 1u : 0u);
           if (kSplit) umma_f16_tmem_a(o, pcol + 32u + ks * 8u, vd, id_o, 1u);
         }
-        umma_commit(smem_addr(&pv_done[t * 2 + (jp & 1)]));
+      };
+      // Each group's commit is issued after this thread's next barrier check,
+      // not before it: a check right behind a commit costs ~300 cycles of
+      // this thread while the queued MMAs drain, one behind plain MMA issues
+      // much less.  A commit tracks every MMA issued before it either way.
+      int pend_t = -1, pend_j = 0;  // P.V of tile pend_t, chunk pend_j: its commits still to issue
+      auto flush = [&]() {
+        if (pend_t >= 0) {
+          umma_commit(smem_addr(&pv_done[pend_t * 2 + (pend_j & 1)]));
+          umma_commit(smem_addr(&kv_empty[pend_j % S]));  // both tiles' P.V of the stage issued
+          pend_t = -1;
+        }
       };
       // S of chunk j+1 (both tiles) is issued before P.V of chunk j, so a
       // tile's softmax of j+1 overlaps the products of chunk j.
       if (ok) ok = mbar_wait_bounded(smem_addr(&kv_full[0]), 0);
       if (ok) {
         tmem_fence_after();
-        issue_qk(0, 0);
-        if (ntiles > 1) issue_qk(1, 0);
+        qk_mmas(0, 0);
+        if (ntiles > 1) qk_mmas(1, 0);
+        umma_commit(smem_addr(&s_full[0]));
+        if (ntiles > 1) umma_commit(smem_addr(&s_full[2]));
       }
       for (int j = 0; j < n_chunks && ok; ++j) {
         const int jn = j + 1;
         if (jn < n_chunks) {
           ok = mbar_test_then_wait(smem_addr(&kv_full[jn % S]), (uint32_t)((jn / S) & 1));
+          flush();
           if (!ok) break;
           // The buffer's previous P (chunk jn - 2) is read by a P.V this
           // thread issued before; tcgen05.mma operations of one thread run in
@@ -407,24 +420,32 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
           // MMAs by the fence after the P wait of that P.V, and K is ordered
           // by its full barrier like any TMA-fed operand.  The tile index is a
           // literal in each call, so the descriptors are fixed at compile time.
-          issue_qk(0, jn);
-          if (ntiles > 1) issue_qk(1, jn);
+          qk_mmas(0, jn);
+          if (ntiles > 1) qk_mmas(1, jn);
+        } else {
+          flush();
         }
         ok = mbar_test_then_wait(smem_addr(&p_full[j & 1]), (uint32_t)((j >> 1) & 1));
-        if (ok) {
-          tmem_fence_after();
-          issue_pv(0, j);
-          if (ntiles > 1) {
-            ok = mbar_test_then_wait(smem_addr(&p_full[2 + (j & 1)]), (uint32_t)((j >> 1) & 1));
-            if (ok) {
-              tmem_fence_after();
-              issue_pv(1, j);
-            }
-          }
+        if (jn < n_chunks) {
+          umma_commit(smem_addr(&s_full[jn & 1]));
+          if (ntiles > 1) umma_commit(smem_addr(&s_full[2 + (jn & 1)]));
         }
         if (!ok) break;
-        umma_commit(smem_addr(&kv_empty[j % S]));
+        tmem_fence_after();
+        pv_mmas(0, j);
+        if (ntiles > 1) {
+          ok = mbar_test_then_wait(smem_addr(&p_full[2 + (j & 1)]), (uint32_t)((j >> 1) & 1));
+          umma_commit(smem_addr(&pv_done[j & 1]));
+          if (!ok) break;
+          tmem_fence_after();
+          pv_mmas(1, j);
+          pend_t = 1;
+        } else {
+          pend_t = 0;
+        }
+        pend_j = j;
       }
+      flush();
       if (!ok) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
     }
     __syncwarp();

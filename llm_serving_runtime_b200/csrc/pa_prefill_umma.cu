@@ -5,29 +5,38 @@
 // are token-major (row r = query token r / G of head h*G + r % G); query token t
 // attends positions 0 .. L - q_len + t.  A CTA owns 256 rows -- two 128-row
 // MMA tiles -- of one (sequence, kv head) and streams the sequence's K/V in
-// 64-token chunks shared by both tiles:
+// 64-token chunks shared by both tiles.  The CTAs of one (sequence, kv head)
+// are adjacent in the grid, so they run in one wave and share K/V through L2.
 //
 //   warp 8 (producer)   TMA-loads each chunk's four 16-token units (K and V, two
-//                       64-column halves each, 128-byte swizzle) into a ring;
+//                       64-column halves each, 128-byte swizzle) into a ring,
+//                       every box of a chunk from its own lane in one
+//                       instruction;
 //   warp 9 (MMA)        one thread issues, per chunk, S_t = Q_t K^T (M=128, N=64,
 //                       K=D) for both tiles into TMEM, then O_t += P_t V
 //                       (M=128, N=D, K=64) with P_t read from TMEM, signalling
-//                       mbarriers with tcgen05.commit;
+//                       mbarriers with tcgen05.commit (each commit after its
+//                       next barrier check: a check right behind a commit
+//                       stalls while the queued MMAs drain);
 //   warps 0-3 / 4-7     softmax of tile 0 / tile 1: thread i owns query row i
 //                       = TMEM lane i; it loads its S row (tcgen05.ld), masks,
 //                       takes the max and exponentials without any cross-thread
 //                       reduction, and writes its P row (bf16: hi and lo parts,
 //                       so P.V keeps ~16 bits of P) back over the same TMEM
 //                       columns (tcgen05.st) as the A operand of the PV MMA;
-//                       finally it reads O back, normalises and stores it.
+//                       finally it reads O back, normalises and stores it;
+//   warp 10             (the cascade's prefix pass only) checks that every
+//                       member reaches the shared prefix through the same
+//                       physical blocks.
 //
 // While one tile's softmax runs, the tensor core works on the other tile's
 // products, so neither waits for the other.  Each tile has two S/P buffers in
 // TMEM; the MMA thread refills a buffer right after issuing the PV that reads
-// its P (the tensor core runs one thread's MMAs in issue order).  The online softmax keeps a reference max per row and rescales O
-// (TMEM load, scale, store) only when a chunk raises the row max by more than
-// 2^8, so p stays below 256 and the arithmetic is exact; most chunks skip the
-// rescale.  Every wait is bounded; TMEM is always released before the CTA exits.
+// its P (the tensor core runs one thread's MMAs in issue order).  The online
+// softmax keeps a reference max per row and rescales O (TMEM load, scale,
+// store) only when a chunk raises the row max by more than 2^8, so p stays
+// below 256 and the arithmetic is exact; most chunks skip the rescale.  Every
+// wait is bounded; TMEM is always released before the CTA exits.
 #include <math.h>
 
 #include "pa_common.cuh"

@@ -76,12 +76,6 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok;
 }
 
-// mbar_wait_bounded that first probes without blocking.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity);
-__device__ __forceinline__ bool mbar_test_then_wait(uint32_t bar, uint32_t parity) {
-  return mbar_test(bar, parity) || mbar_wait_bounded(bar, parity);
-}
-
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
@@ -89,6 +83,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
     if (mbar_try_wait(bar, parity)) return true;
     if (clock64() - t0 > PA_WAIT_LIMIT_CYCLES) return false;
   }
+}
+
+// mbar_wait_bounded that first probes without blocking: for barriers that are
+// usually complete already, the probe is cheaper than a potentially blocking
+// try_wait.
+__device__ __forceinline__ bool mbar_test_then_wait(uint32_t bar, uint32_t parity) {
+  return mbar_test(bar, parity) || mbar_wait_bounded(bar, parity);
 }
 
 // 4-D TMA tile load global -> shared, completion counted on `bar`.

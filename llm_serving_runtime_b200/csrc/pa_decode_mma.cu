@@ -112,12 +112,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kDecodeWarps * stages * STAGE_BYTES);
   int* s_lens = reinterpret_cast<int*>(bars + kDecodeWarps * stages);
   int* s_pref = s_lens + p.B;
+  int* s_rpref = s_pref + p.B + 1;  // exclusive prefix of rows with units, per sequence
   // Cascade (shared prefixes): the prefix kernel has attended each member's
   // first s_u0[b] units; the work list starts every sequence after them.
-  int* s_u0 = s_pref + p.B + 1;
+  int* s_u0 = s_rpref + p.B + 1;
   constexpr bool cascade = kMode == 1;
   constexpr bool gather = kMode == 2;
   __shared__ int s_warp_tot[kDecodeWarps];
+  __shared__ int s_warp_rows[kDecodeWarps];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -141,7 +143,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     const int per = (B + nthr - 1) / nthr;
     const int beg = min(B, tid * per);
     const int end = min(B, beg + per);
-    int local = 0;
+    int local = 0, local_rows = 0;
     for (int b = beg; b < end; ++b) {
       int L = p.context_lens[b] + p.len_offset;
       if (L > cap) {
@@ -156,27 +158,51 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         if (gi >= 0 && gi < p.num_groups) u0 = cascade_prefix_tokens(p, gi) / kUnitTokens;
         s_u0[b] = u0;
       }
-      int units = 0;
-      for (int mg = 0; mg < p.NMG; ++mg) units += max(0, group_units(L, mg, p) - u0);
+      int units = 0, rows = 0;
+      for (int mg = 0; mg < p.NMG; ++mg) {
+        const int n = max(0, group_units(L, mg, p) - u0);
+        units += n;
+        rows += n > 0;
+      }
       local += units * p.Hkv;
+      local_rows += rows * p.Hkv;
     }
-    int incl = local;
+    int incl = local, incl_r = local_rows;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
+      const int vr = __shfl_up_sync(0xffffffffu, incl_r, o);
+      if (lane >= o) {
+        incl += v;
+        incl_r += vr;
+      }
     }
-    if (lane == 31) s_warp_tot[warp] = incl;
+    if (lane == 31) {
+      s_warp_tot[warp] = incl;
+      s_warp_rows[warp] = incl_r;
+    }
     __syncthreads();
-    int run = incl - local;
-    for (int w = 0; w < warp; ++w) run += s_warp_tot[w];
+    int run = incl - local, run_r = incl_r - local_rows;
+    for (int w = 0; w < warp; ++w) {
+      run += s_warp_tot[w];
+      run_r += s_warp_rows[w];
+    }
     for (int b = beg; b < end; ++b) {
       s_pref[b] = run;
-      int units = 0;
-      for (int mg = 0; mg < p.NMG; ++mg) units += max(0, group_units(s_lens[b], mg, p) - (cascade ? s_u0[b] : 0));
+      s_rpref[b] = run_r;
+      int units = 0, rows = 0;
+      for (int mg = 0; mg < p.NMG; ++mg) {
+        const int n = max(0, group_units(s_lens[b], mg, p) - (cascade ? s_u0[b] : 0));
+        units += n;
+        rows += n > 0;
+      }
       run += units * p.Hkv;
+      run_r += rows * p.Hkv;
     }
-    if (tid == nthr - 1) s_pref[B] = run;
+    if (tid == nthr - 1) {
+      s_pref[B] = run;
+      s_rpref[B] = run_r;
+    }
   }
   fence_mbar_init();
   __syncthreads();
@@ -248,12 +274,62 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     finish_warp();
     return;
   }
-  long long nw_eff = (W + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
+  // Slices are equal in cost, not in units: a row (a row group of one
+  // sequence and kv head with units) costs its units plus kRowCostUnits for
+  // what a row start and end take (query load, output store, fold, merge).
+  // Unit u of a row whose cost starts at rc sits at cost position
+  // rc + kRowCostUnits + u; a warp's slice is the units whose positions fall
+  // in its equal share of the total cost C.
+  constexpr int kRowCostUnits = cascade ? kRowCostUnitsCascade : kRowCostUnitsPlain;
+  const long long C = W + (long long)kRowCostUnits * s_rpref[B];
+  long long nw_eff = (C + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
   if (nw_eff > p.nw_total) nw_eff = p.nw_total;
   if (nw_eff < 1) nw_eff = 1;
   const int gw = blockIdx.x * kDecodeWarps + warp;
-  const long long ws = W * gw / nw_eff;
-  const long long we = W * (gw + 1) / nw_eff;
+  auto cost_pref = [&](int b) -> long long { return (long long)s_pref[b] + (long long)kRowCostUnits * s_rpref[b]; };
+  // Cost at which row group mg of kv head h of sequence b starts.
+  auto row_cost_start = [&](int b, int h, int mg) -> long long {
+    const int S = (s_pref[b + 1] - s_pref[b]) / p.Hkv;
+    const int NR = (s_rpref[b + 1] - s_rpref[b]) / p.Hkv;
+    long long x = cost_pref(b) + (long long)h * (S + (long long)kRowCostUnits * NR);
+    for (int m = 0; m < mg; ++m) {
+      const int n = units_of(b, m);
+      if (n > 0) x += n + kRowCostUnits;
+    }
+    return x;
+  };
+  // The first flat unit whose cost position is at least x (W when none).
+  auto unit_at_cost = [&](long long x) -> long long {
+    if (x >= C) return W;
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cost_pref(mid) <= x)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    // lo is the last sequence whose cost starts at or before x: it has units
+    const int S = (s_pref[lo + 1] - s_pref[lo]) / p.Hkv;
+    const int NR = (s_rpref[lo + 1] - s_rpref[lo]) / p.Hkv;
+    const long long Sc = S + (long long)kRowCostUnits * NR;
+    const long long off = x - cost_pref(lo);
+    const int h = (int)(off / Sc);
+    long long o = off - (long long)h * Sc;
+    long long f = s_pref[lo] + (long long)h * S;
+    for (int mg = 0; mg < p.NMG; ++mg) {
+      const int n = units_of(lo, mg);
+      if (n == 0) continue;
+      if (o < n + kRowCostUnits) return f + (o > kRowCostUnits ? o - kRowCostUnits : 0);
+      o -= n + kRowCostUnits;
+      f += n;
+    }
+    return f;
+  };
+  // The warp whose cost share holds position x.
+  auto warp_at_cost = [&](long long x) -> int { return (int)(((x + 1) * nw_eff - 1) / C); };
+  const long long ws = unit_at_cost(C * gw / nw_eff);
+  const long long we = unit_at_cost(C * (gw + 1) / nw_eff);
   if (gw >= nw_eff || ws >= we) {
     finish_warp();
     return;
@@ -544,9 +620,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         __threadfence();
         __syncwarp();
         const long long row_start = cf - cc.u;
-        const long long row_stop = row_start + cc.n;  // exclusive
-        const int gw1 = (int)(((row_start + 1) * nw_eff - 1) / W);
-        const int gw2 = (int)((row_stop * nw_eff - 1) / W);
+        const long long row_cost = row_cost_start(b, h, mg) + kRowCostUnits;  // cost position of its unit 0
+        const int gw1 = warp_at_cost(row_cost);
+        const int gw2 = warp_at_cost(row_cost + cc.n - 1);
         const int npieces = gw2 - gw1 + 1;
         // A split row's counter is indexed by the warp that holds its last unit:
         // that warp starts inside the row, so no other split row ends there.
@@ -558,7 +634,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         if (old == npieces - 1) {
           // Last arrival: log-sum-exp merge of all pieces of this row.
           __threadfence();
-          const bool gw1_first = (W * gw1 / nw_eff) == row_start;
+          const bool gw1_first = unit_at_cost(C * gw1 / nw_eff) == row_start;
           auto slot_ptr = [&](int i) -> const float* {
             const int g2 = gw1 + i;
             const int si = (i == 0 && !gw1_first) ? 2 * g2 + 1 : 2 * g2;
@@ -721,7 +797,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
 size_t decode_mma_smem_bytes(int D, int B, int stages, bool cascade) {
   const size_t stage_bytes = 2u * 16u * (size_t)D * 2u;
   return 1024 + (size_t)kDecodeWarps * stages * stage_bytes + (size_t)kDecodeWarps * stages * 8 +
-         (size_t)((cascade ? 3 : 2) * B + 1) * 4;
+         (size_t)((cascade ? 4 : 3) * B + 2) * 4;
 }
 
 template <typename T, int D, int kMode>

@@ -25,6 +25,11 @@ constexpr int umma_threads(bool prefix) { return (prefix ? 11 : 10) * 32; }
 // Minimum number of 16-token units a warp's share of the flat work list holds
 // before the kernel stops splitting the work further.
 constexpr int kMinUnitsPerWarp = 8;
+// Cost of a row's start and end in the decode kernel's stream-K split, in
+// units: warps whose slices hold many short rows get fewer units.  Under the
+// cascade a row end also folds the row's prefix state.
+constexpr int kRowCostUnitsPlain = 2;
+constexpr int kRowCostUnitsCascade = 2;
 // Split rows of at most this many pieces are merged in the MMA fragment layout
 // (all loads in flight at once); longer ones by the lane-parallel merge.
 constexpr int kFragMergePieces = 4;

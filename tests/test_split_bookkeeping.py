@@ -1,8 +1,10 @@
 """The integer bookkeeping the decode kernel's stream-K split relies on.
 
 The kernel (llm_serving_runtime_b200/csrc/pa_decode_mma.cu) cuts one flat list
-of (sequence, row, 16-token unit) into equal contiguous warp slices and merges
-rows cut by a slice boundary through per-warp partial slots and arrival
+of (sequence, row, 16-token unit) into contiguous warp slices of equal cost --
+a row costs its units plus ROW_COST for its start and end, unit u of a row
+whose cost starts at rc sitting at cost position rc + ROW_COST + u -- and
+merges rows cut by a slice boundary through per-warp partial slots and arrival
 counters.  This test replays that arithmetic in Python over random ragged
 batches and checks the invariants the kernel needs:
   * every split row receives exactly the number of pieces the merger expects
@@ -19,26 +21,41 @@ import random
 import pytest
 
 
-def _warp_of(x, nw, W):
-    return ((x + 1) * nw - 1) // W
+ROW_COST = 2  # kRowCostUnits in csrc/pa_internal.h
 
 
-def simulate(row_units, min_units=8, nw_total=1184):
+def _warp_of(x, nw, C):
+    """The warp whose cost share [C*g//nw, C*(g+1)//nw) holds cost position x."""
+    return ((x + 1) * nw - 1) // C
+
+
+def simulate(row_units, min_units=8, nw_total=1184, row_cost=ROW_COST):
     """row_units: units of each row in flat order (0 = a row with nothing to
     attend, skipped).  Replays the kernel's slicing, piece and merge logic."""
     rows = [n for n in row_units]
-    starts = []
-    acc = 0
+    starts, cstarts = [], []  # flat unit start and cost start of each row
+    acc = cacc = 0
     for n in rows:
         starts.append(acc)
+        cstarts.append(cacc)
         acc += n
-    W = acc
+        cacc += n + (row_cost if n > 0 else 0)
+    W, C = acc, cacc
     if W == 0:
         return []
-    nw = min(nw_total, max(1, (W + min_units - 1) // min_units))
+    nw = min(nw_total, max(1, (C + min_units - 1) // min_units))
+
+    def unit_at_cost(x):  # first flat unit whose cost position is >= x
+        if x >= C:
+            return W
+        for r, n in enumerate(rows):
+            if n > 0 and x < cstarts[r] + row_cost + n:
+                return starts[r] + max(0, x - cstarts[r] - row_cost)
+        return W
+
     counters, slots, owners, problems = {}, {}, {}, []
     for gw in range(nw):
-        ws, we = W * gw // nw, W * (gw + 1) // nw
+        ws, we = unit_at_cost(C * gw // nw), unit_at_cost(C * (gw + 1) // nw)
         if ws >= we:
             continue
         # locate: the row holding flat index ws (rows with 0 units are skipped)
@@ -57,9 +74,16 @@ def simulate(row_units, min_units=8, nw_total=1184):
                     problems.append(("slot reused", si))
                 slots[si] = r
                 counters[r] = counters.get(r, 0) + 1
-                owner = _warp_of(cf - u + n - 1, nw, W)
+                owner = _warp_of(cstarts[r] + row_cost + n - 1, nw, C)
                 if owners.setdefault(owner, r) != r:
                     problems.append(("counter shared", owner))
+                # the merger's choice of the first piece's slot
+                g1 = _warp_of(cstarts[r] + row_cost, nw, C)
+                if row_end and counters[r] == owner - g1 + 1:
+                    g1_first = unit_at_cost(C * g1 // nw) == starts[r]
+                    want = 2 * g1 + (0 if g1_first else 1)
+                    if slots.get(want) != r:
+                        problems.append(("first slot", r, want))
             u += 1
             if u == n:  # advance to the next row with units
                 u = 0
@@ -68,8 +92,8 @@ def simulate(row_units, min_units=8, nw_total=1184):
                     r += 1
             cf += 1
     for r, c in counters.items():
-        n, rs = rows[r], starts[r]
-        expected = _warp_of(rs + n - 1, nw, W) - _warp_of(rs, nw, W) + 1
+        n = rows[r]
+        expected = _warp_of(cstarts[r] + row_cost + n - 1, nw, C) - _warp_of(cstarts[r] + row_cost, nw, C) + 1
         if c != expected:
             problems.append(("piece count", r, c, expected))
     return problems
@@ -90,11 +114,12 @@ def _decode_rows(rng, B, Hkv, groups):
 
 
 @pytest.mark.parametrize("seed", range(6))
-def test_split_bookkeeping_invariants(seed):
+@pytest.mark.parametrize("row_cost", [ROW_COST, 0, 5])
+def test_split_bookkeeping_invariants(seed, row_cost):
     rng = random.Random(seed)
     for _ in range(150):
         rows = _decode_rows(rng, rng.randint(1, 24), rng.choice([1, 2, 8]), rng.choice([1, 2, 4]))
-        assert simulate(rows, nw_total=rng.choice([8, 64, 1184])) == []
+        assert simulate(rows, nw_total=rng.choice([8, 64, 1184]), row_cost=row_cost) == []
 
 
 def test_ragged_rows_with_empty_ones():

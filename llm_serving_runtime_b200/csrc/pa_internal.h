@@ -28,8 +28,8 @@ constexpr int kMinUnitsPerWarp = 8;
 // Cost of a row's start and end in the decode kernel's stream-K split, in
 // units: warps whose slices hold many short rows get fewer units.  Under the
 // cascade a row end also folds the row's prefix state.
-constexpr int kRowCostUnitsPlain = 2;
-constexpr int kRowCostUnitsCascade = 2;
+constexpr int kRowCostUnitsPlain = 1;
+constexpr int kRowCostUnitsCascade = 4;
 // Split rows of at most this many pieces are merged in the MMA fragment layout
 // (all loads in flight at once); longer ones by the lane-parallel merge.
 constexpr int kFragMergePieces = 4;

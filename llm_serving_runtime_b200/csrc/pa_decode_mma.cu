@@ -9,9 +9,10 @@
 //
 // How (B200-first):
 //  * Work is one flat list of 16-token "units" ordered (sequence, kv head,
-//    query-row group, unit).  Every warp of the persistent grid takes an equal,
-//    contiguous slice of it (stream-K), so ragged / log-uniform lengths balance
-//    to within one unit.  A slice that covers a whole (sequence, head) writes
+//    query-row group, unit).  Every warp of the persistent grid takes a
+//    contiguous slice of it of equal cost (stream-K), a row costing its units
+//    plus a fixed few for its start and end, so ragged / log-uniform lengths
+//    and many short rows balance alike.  A slice that covers a whole (sequence, head) writes
 //    the output directly; a row cut by a slice boundary leaves (m, l, acc)
 //    partials in the workspace, and the last warp to finish that row merges
 //    them with a log-sum-exp reduction (arrival counter, reset after use; one

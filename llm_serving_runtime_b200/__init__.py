@@ -7,6 +7,8 @@ Public entry points
   kv_append(...)                      the KV-append kernel alone
   prefix_sharing.PrefixGroups         shared prompt prefixes -> cascade decode
                                       (paged_attention_decode(..., prefix_groups=))
+  shared_blocks.BlockRefAllocator     refcounted KV blocks: prefix-cache snapshots and
+                                      hits share blocks instead of copying them
   reference_api                       drop-in for runtime/phase2/paged_attention_triton.py
   kv_block_pool.GpuKVBlockPool        drop-in for runtime/phase2/paged_kv_kernel.py
   block_paged_attention               drop-in HF attention hook

@@ -283,3 +283,66 @@ def test_reference_prefix_cache_on_zero_copy_snapshots(reference_prefix_cache):
     assert alloc.stats()["used_blocks"] == len(b.block_ids)  # the borrower keeps its prefix alive
     alloc.free_request("b")
     assert alloc.stats()["free_blocks"] == 40
+
+
+def test_reference_counts_stay_consistent_under_random_sharing():
+    """Seeded random mix of allocations, growth, snapshots, borrowing,
+    copy-on-write, releases and frees.  After every call each block's count
+    equals the holders that name it, and a block is free exactly when nobody
+    holds it; at the end every block comes back."""
+    import random
+
+    rng = random.Random(2024)
+    bs, total = 4, 64
+    alloc = BlockRefAllocator(total_blocks=total, block_size_tokens=bs)
+    entries: list[list[int]] = []
+    live: list[str] = []
+    n_req = 0
+
+    def check():
+        holders: dict[int, int] = {}
+        for rid in live:
+            for b in alloc.get_request_allocation(rid).block_ids:
+                holders[b] = holders.get(b, 0) + 1
+        for e in entries:
+            for b in e:
+                holders[b] = holders.get(b, 0) + 1
+        for b in range(total):
+            assert alloc.ref_count(b) == holders.get(b, 0), b
+            assert (b in alloc._free_set) == (b not in holders), b
+        assert len(alloc._free) == len(alloc._free_set) == total - len(holders)
+
+    for _ in range(3000):
+        r = rng.random()
+        if r < 0.25 or not live:
+            borrowed = rng.choice(entries) if entries and rng.random() < 0.6 else None
+            a = alloc.allocate_for_tokens(f"q{n_req}", rng.randint(1, 10 * bs), borrowed_block_ids=borrowed)
+            if a is not None:
+                live.append(a.request_id)
+            n_req += 1
+        elif r < 0.35:
+            alloc.allocate_for_tokens(rng.choice(live), rng.randint(1, 14 * bs))
+        elif r < 0.5:
+            a = alloc.get_request_allocation(rng.choice(live))
+            n = rng.randint(1, len(a.block_ids))
+            entries.append(alloc.snapshot_blocks(a.block_ids[:n]))
+        elif r < 0.65:
+            a = alloc.get_request_allocation(rng.choice(live))
+            cap = len(a.block_ids) * bs
+            start = rng.randrange(cap)
+            alloc.make_writable(a.request_id, start, rng.randint(1, cap - start), lambda s, d: None)
+        elif r < 0.8 and entries:
+            alloc.release_blocks(entries.pop(rng.randrange(len(entries))))
+        else:
+            alloc.free_request(live.pop(rng.randrange(len(live))), reason="cancel")
+        check()
+    s = alloc.stats()
+    assert s["cow_copies_total"] > 0 and s["borrowed_blocks_total"] > 0 and s["snapshot_blocks_total"] > 0
+    for rid in live:
+        alloc.free_request(rid)
+    for e in entries:
+        alloc.release_blocks(e)
+    live.clear()
+    entries.clear()
+    check()
+    assert alloc.stats()["free_blocks"] == total

@@ -465,7 +465,8 @@ def main() -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
-    ratio = _traffic_ratio_from_profiles(args.workload)
+    # a cascade call moves other bytes than the plain call on the same workload
+    ratio = _traffic_ratio_from_profiles(args.workload + ("+cascade" if pg is not None else ""))
     traffic = None if (ratio is None or tensor_bound) else ratio * dec_bytes
     line = {
         "metric": METRIC,

@@ -71,6 +71,8 @@ CASES = [
     ([2, 2], [128, 96], 1, [128, 300, 96, 97, 10], 8, 2, 128, 16, torch.bfloat16, 1),
     ([3], [256], 0, [300, 256, 999], 64, 8, 128, 16, torch.bfloat16, 2),           # G = 8
     ([3, 2], [256, 128], 1, [256, 300, 500, 128, 200, 60], 32, 8, 80, 16, torch.bfloat16, 2),  # head_dim 80
+    ([3, 2], [256, 128], 1, [256, 300, 700, 128, 200, 60], 32, 8, 128, 64, torch.bfloat16, 1),  # 64-token blocks
+    ([4], [512], 0, [512, 600, 1000, 530], 32, 8, 128, 128, torch.float16, 2),  # 128-token blocks
 ]
 
 

@@ -35,6 +35,9 @@ CASES = [
     # head_dim 80 / 96 (padded to 128 tiles), on the multi-query kernels
     (10, 32, 8, 80, 16, torch.bfloat16, [0, 50, 300, 1000, 17, 0, 2000, 64, 5, 700], 256),
     (12, 14, 2, 96, 16, torch.float16, [1, 2, 3, 900, 100, 0, 33, 64, 65, 500, 8, 1200], 640),
+    # 64- and 128-token blocks on the tcgen05 multi-query kernel
+    (10, 32, 8, 128, 64, torch.bfloat16, [0, 50, 300, 1000, 17, 0, 2000, 64, 5, 700], 256),
+    (10, 32, 8, 128, 128, torch.float16, [0, 50, 300, 1000, 17, 0, 2000, 64, 5, 700], 256),
 ]
 
 

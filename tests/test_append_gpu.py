@@ -111,3 +111,32 @@ def test_non_contiguous_new_rows():
     k2, v2 = w.key_cache.clone(), w.value_cache.clone()
     kv_append(w.new_key, w.new_value, k2, v2, w.slot_mapping)
     assert torch.equal(k1, k2) and torch.equal(v1, v2)
+
+
+@pytest.mark.parametrize("bs,D,dtype", [(4, 64, torch.float32), (8, 128, torch.bfloat16), (32, 96, torch.float16),
+                                        (64, 128, torch.bfloat16), (128, 64, torch.float16),
+                                        (256, 128, torch.bfloat16)])
+def test_append_bit_exact_across_block_sizes(bs, D, dtype):
+    """Both forms of the append (explicit slots; block tables + positions) at
+    every block size the decode kernels take, against the oracle's scatter."""
+    g = torch.Generator().manual_seed(bs * 7 + D)
+    B, Hkv, q_len, nb = 5, 4, 3, 16
+    kc = torch.randn(nb, Hkv, bs, D, generator=g).to(dtype)
+    vc = torch.randn(nb, Hkv, bs, D, generator=g).to(dtype)
+    nk = torch.randn(B, Hkv, q_len, D, generator=g).to(dtype)
+    nv = torch.randn(B, Hkv, q_len, D, generator=g).to(dtype)
+    slots = torch.randperm(nb * bs, generator=g)[:B * q_len].to(torch.int64)
+    kc_d, vc_d = kc.to(DEV), vc.to(DEV)
+    kv_append(nk.to(DEV), nv.to(DEV), kc_d, vc_d, slots.to(DEV), validate=True)
+    ref_k, ref_v = kc.clone(), vc.clone()
+    oracle.kv_append(nk, nv, ref_k, ref_v, slots)
+    assert torch.equal(_bits(kc_d), _bits(ref_k)) and torch.equal(_bits(vc_d), _bits(ref_v))
+
+    # rows own 3 blocks each; a write may cross a block boundary
+    tables = torch.randperm(nb, generator=g)[:B * 3].reshape(B, 3).to(torch.int32)
+    starts = torch.randint(0, 3 * bs - q_len + 1, (B,), generator=g).to(torch.int64)
+    kv_append(nk.to(DEV), nv.to(DEV), kc_d, vc_d, block_tables=tables.to(DEV), positions=starts.to(DEV),
+              validate=True)
+    derived = oracle.slot_mapping_from_tables(tables, starts, q_len, bs)
+    oracle.kv_append(nk, nv, ref_k, ref_v, derived)
+    assert torch.equal(_bits(kc_d), _bits(ref_k)) and torch.equal(_bits(vc_d), _bits(ref_v))

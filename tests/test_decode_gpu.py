@@ -140,6 +140,7 @@ EDGE = [
     (3, 8, 2, 128, 128, torch.bfloat16, [127, 128, 1000], 1),    # block size 128
     (3, 32, 8, 128, 256, torch.float16, [255, 256, 2000], 2),     # block size 256
     (4, 8, 2, 64, 4, torch.float32, [0, 3, 4, 77], 1),            # fp32, block size 4
+    (3, 8, 2, 64, 128, torch.float32, [100, 128, 700], 1),       # fp32, block size 128
     (3, 8, 2, 128, 16, torch.float32, [10, 31, 300], 4),          # fp32, causal
     (2, 4, 2, 32, 16, torch.float32, [5, 64], 1),                 # fp32, head_dim 32
 ]

@@ -38,6 +38,8 @@ CASES = [
     # 64- and 128-token blocks on the tcgen05 multi-query kernel
     (10, 32, 8, 128, 64, torch.bfloat16, [0, 50, 300, 1000, 17, 0, 2000, 64, 5, 700], 256),
     (10, 32, 8, 128, 128, torch.float16, [0, 50, 300, 1000, 17, 0, 2000, 64, 5, 700], 256),
+    # long cached contexts: a 256-token chunk over up to 16k cached tokens
+    (4, 32, 8, 128, 16, torch.bfloat16, [16000, 5, 9000, 12000], 256),
 ]
 
 

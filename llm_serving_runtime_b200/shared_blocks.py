@@ -58,7 +58,12 @@ class Allocation:
 
 
 class BlockRefAllocator:
-    """Paged KV block allocator whose blocks are held by reference count."""
+    """Paged KV block allocator whose blocks are held by reference count.
+
+    Not thread-safe, like the reference's: the worker calls it from its one
+    scheduler thread (worker_server.py:1298).  ``make_writable``'s copy runs on
+    the caller's current CUDA stream before the append that follows it there.
+    """
 
     def __init__(self, total_blocks: int, block_size_tokens: int, bytes_per_token: int = 1) -> None:
         if total_blocks <= 0:

@@ -228,10 +228,18 @@ typedef struct pa_gather_args {
   int64_t wait_ns;               /* bound on the wait for the other ranks' flags */
 } pa_gather_args;
 
+/* The ranks of a fused gather fell out of step: a wait ran out, or a peer's
+ * flag skipped calls.  The rank that sees it sets bit 31 of its epoch and of
+ * its flag at every rank, so every later pa_decode_gather call on every rank
+ * reports this bit at once, without waiting, until the ranks start again from
+ * fresh (zeroed) flags and epochs. */
+#define PA_DEVERR_GATHER 0x20u
+
 /* pa_decode for the local KV heads, output rows written to every rank's gathered
  * output at query-head offset head_offset (args->out_stride_* are the gathered
  * output's strides).  fp16/bf16 only.  A rank whose flag does not arrive in time
- * is reported as PA_DEVERR_WAIT_TIMEOUT; no wait is unbounded. */
+ * is reported as PA_DEVERR_WAIT_TIMEOUT | PA_DEVERR_GATHER; no wait is
+ * unbounded. */
 PA_API int pa_decode_gather(const pa_decode_args* args, const pa_gather_args* gather, void* stream);
 
 /* Size of the scratch array behind pa_decode_static_workspace (16 MiB). */
@@ -241,14 +249,16 @@ PA_API int pa_decode_gather(const pa_decode_args* args, const pa_gather_args* ga
  * the reference (its decode allocates scratch on first use per shape).
  * Takes the same arguments as pa_decode but ignores args->workspace and
  * args->workspace_bytes: the scratch is a 16 MiB __device__ array inside this
- * library, which every GPU that loads the library holds until the process
- * exits.  Nothing is allocated: a plugin host that hands its kernels only
- * inputs and outputs, or a serving loop that has given all free HBM to the KV
- * pool, can call it.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress, that device current) and should come before
- * any stream capture.  Every call shares the array: each clears the error word
- * and merge counters on its stream before the decode, and calls that overlap
- * on the GPU race.  Shapes needing more scratch than PA_STATIC_WORKSPACE_BYTES
+ * library.  The CUDA runtime loads device code lazily, so the array is created
+ * in a GPU's memory by the first call on that GPU and held there until the
+ * process exits; that first call also looks up the array's device address
+ * (cudaGetSymbolAddress, that device current).  Make it before giving the rest
+ * of the free memory to the KV pool and before any stream capture.  After it,
+ * nothing is allocated: a plugin host that hands its kernels only inputs and
+ * outputs, or a serving loop that has given all free HBM to the KV pool, can
+ * call it.  Every call shares the array: each clears the error word and merge
+ * counters on its stream before the decode, and calls that overlap on the GPU
+ * race.  Shapes needing more scratch than PA_STATIC_WORKSPACE_BYTES
  * (pa_decode_workspace_bytes) are rejected with PA_ERR_WORKSPACE; on a 148-SM
  * B200 that is more than 13 query rows per KV head (G * q_len) at head_dim 128.
  * The kernels still skip invalid block ids, but their device error word stays

@@ -10,9 +10,10 @@ Public entry points
   shared_blocks.BlockRefAllocator     refcounted KV blocks: prefix-cache snapshots and
                                       hits share blocks instead of copying them
   reference_api                       drop-in for runtime/phase2/paged_attention_triton.py
-  kv_block_pool.GpuKVBlockPool        drop-in for runtime/phase2/paged_kv_kernel.py
-  block_paged_attention               drop-in HF attention hook
-  integration.install()               patch the reference runtime in place
+  kv_block_pool.write_tokens_batch_into
+                                      the reference pool's write_tokens_batch on the append kernel
+  integration.install()               patch the reference runtime in place (decode, append,
+                                      and multi-token steps through its cache and HF hook)
 
 The kernels live in lib/libpa_b200.so (C ABI: include/paged_attention_b200.h).
 """

@@ -28,6 +28,7 @@ PA_DEVERR_TABLE_UNDERRUN = 0x2
 PA_DEVERR_SLOT_RANGE = 0x4
 PA_DEVERR_WAIT_TIMEOUT = 0x8
 PA_DEVERR_PREFIX = 0x10
+PA_DEVERR_GATHER = 0x20
 
 PA_STATIC_WORKSPACE_BYTES = 16 << 20
 

@@ -62,12 +62,30 @@ __device__ __forceinline__ int group_units(int L, int mg, const DecodeParams& p)
 // and wait, at most p.wait_ns, until every rank's flag in this rank's array
 // reached the epoch.  The other ranks' output rows in this rank's gathered
 // output are visible once their flags are (each warp fenced its stores before
-// counting itself done).
+// counting itself done).  A peer's flag may already be one call ahead (it
+// finished the next call, whose rows go to the other gathered buffer); more
+// than one is impossible while the ranks make the same calls.
+//
+// Once a wait runs out, or a peer's flag is out of step, the ranks no longer
+// agree on which call is which, and a later call could take a peer's rows of a
+// different call without noticing.  So the rank poisons the gather: bit 31 of
+// its epoch and of its flag at every rank.  Every later call of this rank, and
+// of every peer that reads the flag, then reports PA_DEVERR_GATHER at once,
+// without waiting, until the ranks set up fresh flags together.
+constexpr uint32_t kGatherPoison = 0x80000000u;
+
 __device__ __noinline__ void gather_barrier(uint32_t* const* flags_ranks, uint32_t* epoch, uint32_t* done_warps,
                                             int n_ranks, int rank, int64_t wait_ns, uint32_t* status, int lane) {
   __threadfence();
-  const uint32_t e = *epoch + 1u;
+  const uint32_t cur = *epoch;
   __syncwarp();
+  if (cur & kGatherPoison) {
+    if (lane == 0) *done_warps = 0u;
+    for (int i = lane; i < n_ranks; i += 32) st_release_sys(flags_ranks[i] + rank, cur);
+    if (lane == 0) raise_flag(status, PA_DEVERR_GATHER);
+    return;
+  }
+  const uint32_t e = (cur + 1u) & ~kGatherPoison;
   if (lane == 0) {
     *done_warps = 0u;  // ready for the next call
     *epoch = e;
@@ -75,18 +93,36 @@ __device__ __noinline__ void gather_barrier(uint32_t* const* flags_ranks, uint32
   __threadfence_system();
   for (int i = lane; i < n_ranks; i += 32) st_release_sys(flags_ranks[i] + rank, e);
   const uint32_t* mine = flags_ranks[rank];
-  bool ok = true;
+  bool timed_out = false, out_of_step = false;
   for (int i = lane; i < n_ranks; i += 32) {
     const uint64_t t0 = global_ns();
-    while ((int)(ld_acquire_sys(mine + i) - e) < 0) {
+    for (;;) {
+      const uint32_t f = ld_acquire_sys(mine + i);
+      const uint32_t d = (f - e) & ~kGatherPoison;
+      if (f & kGatherPoison) {
+        out_of_step = true;
+        break;
+      }
+      if (d <= 1u) break;  // this call, or the peer is one call ahead
+      if (d < (kGatherPoison >> 1)) {  // ahead by more than one call
+        out_of_step = true;
+        break;
+      }
       if (global_ns() - t0 > (uint64_t)wait_ns) {
-        ok = false;
+        timed_out = true;
         break;
       }
       __nanosleep(256);
     }
   }
-  if (!__all_sync(0xffffffffu, ok) && lane == 0) raise_flag(status, PA_DEVERR_WAIT_TIMEOUT);
+  const bool any_timeout = __any_sync(0xffffffffu, timed_out);
+  if (__any_sync(0xffffffffu, timed_out || out_of_step)) {
+    const uint32_t poisoned = e | kGatherPoison;
+    if (lane == 0) *epoch = poisoned;
+    __threadfence_system();
+    for (int i = lane; i < n_ranks; i += 32) st_release_sys(flags_ranks[i] + rank, poisoned);
+    if (lane == 0) raise_flag(status, PA_DEVERR_GATHER | (any_timeout ? PA_DEVERR_WAIT_TIMEOUT : 0u));
+  }
 }
 
 // kMode 1 (cascade): the call carries shared-prefix groups (pa_decode_cascade);

@@ -9,16 +9,19 @@
 // them from a fixed scratch array that lives inside this library.
 //
 // The array is a file-scope __device__ variable of PA_STATIC_WORKSPACE_BYTES
-// (16 MiB).  Every GPU that loads the library holds it until the process exits.
+// (16 MiB).  The CUDA runtime loads a library's device code lazily by default,
+// so the array is created in a device's memory by the first call on that device
+// (the address lookup below) and then stays there until the process exits.
 // Host code cannot use the array's name as a device address (there it is only a
-// host-side stand-in), so the first call on each device looks the device address
-// up with cudaGetSymbolAddress, with that device current, and caches it; that
-// first call should therefore come before any stream capture.  Every call
-// shares the one array and it keeps the previous call's contents: each call
-// clears the part that must start at zero (error word and merge counters) on
-// its stream, and calls whose kernels overlap on the GPU (other streams) race
-// on it.  Nothing here allocates: no cudaMalloc, cudaFree or allocating library
-// routine is called.
+// host-side stand-in), so that first call looks the device address up with
+// cudaGetSymbolAddress, with the device current, and caches it.  Make the first
+// call on each device before handing the rest of its free memory to the KV pool,
+// and before any stream capture; later calls need no free device memory.  Every
+// call shares the one array and it keeps the previous call's contents: each
+// call clears the part that must start at zero (error word and merge counters)
+// on its stream, and calls whose kernels overlap on the GPU (other streams)
+// race on it.  Nothing here allocates: no cudaMalloc, cudaFree or allocating
+// library routine is called.
 #include <stdio.h>
 
 #include <mutex>
@@ -61,14 +64,28 @@ extern "C" PA_API int pa_decode_static_workspace(const pa_decode_args* args, voi
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return pa::set_last_error(PA_ERR_CUDA, "cudaGetDevice failed");
+  int num_sms = 0;
+  e = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) {
+    char msg[256];
+    snprintf(msg, sizeof(msg), "cudaDeviceGetAttribute(SM count): %s", cudaGetErrorString(e));
+    return pa::set_last_error(PA_ERR_CUDA, msg);
+  }
   void* ws = nullptr;
   int st = static_workspace_address(dev, &ws);
   if (st != PA_OK) return st;
 
+  if (args->num_q_heads <= 0 || args->num_kv_heads <= 0 || args->q_len <= 0 || args->head_dim <= 0 ||
+      args->batch < 0 || args->num_q_heads % args->num_kv_heads != 0)
+    return pa_decode(args, stream);  // pa_decode reports the shape error itself
   const size_t need = pa_decode_workspace_bytes(args->batch, args->num_q_heads, args->num_kv_heads,
                                                 args->q_len, args->head_dim, args->dtype, dev);
-  if (need == 0)
-    return pa::set_last_error(PA_ERR_INVALID_ARGUMENT, "invalid decode shape (heads, q_len or head_dim)");
+  if (need == 0) {
+    // the shape is valid, so the sizing failed on a device query
+    char msg[256];
+    snprintf(msg, sizeof(msg), "sizing the decode scratch on device %d failed: %s", dev, pa_last_error());
+    return pa::set_last_error(PA_ERR_CUDA, msg);
+  }
   if (need > PA_STATIC_WORKSPACE_BYTES) {
     char msg[256];
     snprintf(msg, sizeof(msg),
@@ -79,9 +96,6 @@ extern "C" PA_API int pa_decode_static_workspace(const pa_decode_args* args, voi
   }
 
   // Error word and merge counters must start at zero.
-  int num_sms = 0;
-  e = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return pa::set_last_error(PA_ERR_CUDA, "cudaDeviceGetAttribute(SM count) failed");
   const size_t zero_bytes = pa::kWsHeaderBytes + pa::ws_counter_bytes(num_sms * pa::kDecodeWarps);
   e = cudaMemsetAsync(ws, 0, zero_bytes, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return pa::set_last_error(PA_ERR_CUDA, "cudaMemsetAsync(static workspace) failed");

@@ -29,6 +29,17 @@ Every call launches hand-written sm_100a kernels from ``lib/libpa_b200.so``
 through its C ABI; there is no Triton and no CPU fallback.  No call allocates
 device memory except the first one on a device (or a larger shape), which sizes
 the shared workspace — make that call before capturing a CUDA graph.
+
+Bad inputs (a block id outside the pool, a block table too short for its
+length, a slot outside the pool) never fault: the kernels skip the access and
+set a bit in the workspace's device error word.  After each call an
+asynchronous copy of that word lands in pinned host memory, and the next call
+on the same workspace raises ``IndexError`` (the reference's error,
+runtime/phase2/paged_kv_kernel.py:118-119, :221-222) once the copy shows a bit
+— no host synchronisation on the normal path.  ``validate=True`` (or
+``PA_B200_VALIDATE=1``) checks synchronously at the end of the call instead;
+``validate=False`` skips the check.  Calls under CUDA-graph capture are not
+checked (``read_device_errors`` reads the word after a replay).
 """
 
 from __future__ import annotations
@@ -48,6 +59,7 @@ __all__ = [
     "decode_workspace",
     "read_device_errors",
     "describe_device_errors",
+    "device_error",
     "DeviceErrorFlags",
 ]
 
@@ -64,6 +76,18 @@ class DeviceErrorFlags:
     SLOT_RANGE = _lib.PA_DEVERR_SLOT_RANGE
     WAIT_TIMEOUT = _lib.PA_DEVERR_WAIT_TIMEOUT
     PREFIX = _lib.PA_DEVERR_PREFIX
+    GATHER = _lib.PA_DEVERR_GATHER
+
+
+def device_error(flags: int) -> Exception:
+    """The exception for a non-zero device error word: IndexError for invalid
+    block ids, slots, underruns and prefix groups (the reference's error for
+    them); RuntimeError when only a bounded wait ran out or a fused gather fell
+    out of step."""
+    text = describe_device_errors(flags)
+    index_bits = (DeviceErrorFlags.BLOCK_ID_RANGE | DeviceErrorFlags.TABLE_UNDERRUN | DeviceErrorFlags.SLOT_RANGE
+                  | DeviceErrorFlags.PREFIX)
+    return IndexError(text) if flags & index_bits else RuntimeError(text)
 
 
 def describe_device_errors(flags: int) -> str:
@@ -75,9 +99,11 @@ def describe_device_errors(flags: int) -> str:
     if flags & DeviceErrorFlags.SLOT_RANGE:
         parts.append("slot outside the pool")
     if flags & DeviceErrorFlags.WAIT_TIMEOUT:
-        parts.append("bounded wait on a bulk copy timed out")
+        parts.append("a bounded wait timed out (on a bulk copy, or on a peer rank of a fused gather)")
     if flags & DeviceErrorFlags.PREFIX:
         parts.append("prefix group does not match its members' block tables or bounds")
+    if flags & DeviceErrorFlags.GATHER:
+        parts.append("fused gather ranks out of step (close() on every rank, then start again)")
     return "; ".join(parts)
 
 
@@ -115,10 +141,18 @@ def decode_workspace(device: torch.device, nbytes: int = 256) -> torch.Tensor:
 
 def read_device_errors(device: torch.device | None = None, *, clear: bool = True,
                        workspace: torch.Tensor | None = None) -> int:
-    """Read (and clear) the PA_DEVERR_* bits the kernels recorded.  Synchronises."""
+    """Read (and clear) the PA_DEVERR_* bits the kernels recorded.  Synchronises.
+
+    Clearing also drops the copy of the word that the next call would have
+    checked: the bits it holds have been read here."""
     if workspace is None:
         device = device or torch.device("cuda", torch.cuda.current_device())
         workspace = decode_workspace(device)
+    if clear:
+        with _checks_lock:
+            c = _checks.get((workspace.device.index, workspace.data_ptr()))
+            if c is not None:
+                c.pending = False
     flags = ctypes.c_uint32(0)
     _lib.check(
         _lib.load().pa_read_device_errors(
@@ -127,6 +161,64 @@ def read_device_errors(device: torch.device | None = None, *, clear: bool = True
         "pa_read_device_errors",
     )
     return int(flags.value)
+
+
+class _PendingCheck:
+    """One in-flight copy of a device error word into pinned host memory."""
+
+    __slots__ = ("host", "stream", "after_call", "landed", "pending")
+
+    def __init__(self, device: torch.device):
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.stream = torch.cuda.Stream(device)
+        self.after_call = torch.cuda.Event()
+        self.landed = torch.cuda.Event()
+        self.pending = False
+
+
+_checks_lock = threading.Lock()
+_checks: dict[tuple[int, int], _PendingCheck] = {}
+
+
+def _capturing() -> bool:
+    return torch.cuda.is_current_stream_capturing()
+
+
+def _raise_landed_errors(word: torch.Tensor) -> None:
+    """Raise for the device errors of earlier calls on ``word`` whose copy has
+    landed (the word is read again and cleared, synchronously, only then)."""
+    with _checks_lock:
+        c = _checks.get((word.device.index, word.data_ptr()))
+        if c is None or not c.pending or not c.landed.query():
+            return
+        c.pending = False
+        seen = int(c.host.item())
+    if seen:
+        flags = seen | read_device_errors(workspace=word, clear=True)
+        raise device_error(flags)
+
+
+def _copy_after_call(word: torch.Tensor, stream: torch.cuda.Stream) -> None:
+    """Queue a copy of ``word`` to pinned host memory behind the work on
+    ``stream`` (on a side stream, so ``stream`` is not held up).  While one copy
+    is in flight no other is queued: the word keeps its bits until read, so the
+    next copy covers every call since."""
+    key = (word.device.index, word.data_ptr())
+    with _checks_lock:
+        c = _checks.get(key)
+        if c is None:
+            if len(_checks) >= 64:
+                _checks.pop(next(iter(_checks)))
+            c = _checks[key] = _PendingCheck(word.device)
+        if c.pending:
+            return
+        c.after_call.record(stream)
+        c.stream.wait_event(c.after_call)
+        with torch.cuda.stream(c.stream):
+            c.host.copy_(word[:4].view(torch.int32), non_blocking=True)
+        word.record_stream(c.stream)  # a replaced workspace stays allocated until the copy has run
+        c.landed.record(c.stream)
+        c.pending = True
 
 
 def _cache_view(t: torch.Tensor) -> CacheView:
@@ -219,7 +311,8 @@ def kv_append(
     With ``slot_mapping`` (int64 [B*q_len]) token b*q_len+t goes to that slot;
     otherwise to block_tables[b, p // bs] at offset p % bs with
     p = positions[b] + position_offset + t.  Bit-exact.  Invalid slots or block
-    ids are skipped and flagged (``validate=True`` raises IndexError).
+    ids are skipped and flagged; the next call on the same error word raises
+    IndexError (``validate=True``: this call, synchronously).
     """
     _check_cache_pair(key_cache, value_cache)
     device = key_cache.device
@@ -272,12 +365,17 @@ def kv_append(
     if error_word is None:
         error_word = decode_workspace(device)
     args.error_flags = error_word.data_ptr()
+    deferred = validate is None and not _VALIDATE_DEFAULT and not _capturing()
+    if deferred:
+        _raise_landed_errors(error_word)
     with _with_device(device):
         _lib.check(_lib.load().pa_kv_append(ctypes.byref(args), _stream_ptr(device)), "pa_kv_append")
-    if validate if validate is not None else _VALIDATE_DEFAULT:
+    if deferred:
+        _copy_after_call(error_word, torch.cuda.current_stream(device))
+    elif validate if validate is not None else _VALIDATE_DEFAULT:
         flags = read_device_errors(workspace=error_word)
         if flags:
-            raise IndexError(describe_device_errors(flags))
+            raise device_error(flags)
 
 
 def _cascade_workspace_bytes(B: int, Hq: int, Hkv: int, q_len: int, D: int, dcode: int, dev_index: int,
@@ -370,6 +468,9 @@ def paged_attention_decode(
         need = _workspace_bytes(B, Hq, Hkv, q_len, D, dcode, device.index)
     if workspace is None:
         workspace = decode_workspace(device, need)
+    deferred = validate is None and not _VALIDATE_DEFAULT and not _capturing()
+    if deferred:
+        _raise_landed_errors(workspace)
 
     appended = False
     if key is not None:
@@ -410,8 +511,10 @@ def paged_attention_decode(
                        "pa_decode_cascade")
         else:
             _lib.check(lib.pa_decode(ctypes.byref(args), _stream_ptr(device)), "pa_decode")
-    if validate if validate is not None else _VALIDATE_DEFAULT:
+    if deferred:
+        _copy_after_call(workspace, torch.cuda.current_stream(device))
+    elif validate if validate is not None else _VALIDATE_DEFAULT:
         flags = read_device_errors(workspace=workspace)
         if flags:
-            raise IndexError(describe_device_errors(flags))
+            raise device_error(flags)
     return out

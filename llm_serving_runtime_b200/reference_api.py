@@ -64,7 +64,7 @@ _decode_batch_metadata: contextvars.ContextVar[PagedDecodeBatchMetadata | None] 
 class PagedDecodeBatchMetadata:
     """Batched decode metadata passed explicitly to the kernel."""
 
-    pool: Any  # GpuKVBlockPool (ours or the reference's)
+    pool: Any  # the reference's GpuKVBlockPool, or any pool with k_layer_view / v_layer_view
     layer_idx: int
     block_tables: torch.Tensor  # [B, max_blocks] int32
     seq_lens: torch.Tensor  # [B] int32 — KV length to attend over (includes current token)
@@ -135,7 +135,6 @@ def paged_attention_decode_batched(
     if query.shape[0] != metadata.block_tables.shape[0]:
         raise ValueError("query batch size must match block_tables rows")
     pool = metadata.pool
-    pool._ensure_pools()
     k_layer = pool.k_layer_view(metadata.layer_idx)
     v_layer = pool.v_layer_view(metadata.layer_idx)
     if not query.is_cuda:
@@ -164,7 +163,6 @@ def paged_attention_verify_batched(
     if query.dim() != 4 or query.shape[0] != metadata.block_tables.shape[0]:
         raise ValueError("query must be [batch, heads, k, dim] with the batch of block_tables")
     pool = metadata.pool
-    pool._ensure_pools()
     k_layer = pool.k_layer_view(metadata.layer_idx)
     v_layer = pool.v_layer_view(metadata.layer_idx)
     if query.shape[1] != num_kv_groups * k_layer.shape[1]:

@@ -60,7 +60,8 @@ class HeadShardedDecode:
     ``decode_fn`` computes the local heads' attention (defaults to the sm_100a
     op); the per-rank outputs [B, Hq/N, q, D] are all-gathered into a
     [N, B, Hq/N, q, D] buffer and returned as a [B, Hq, q, D] tensor in the
-    global head order (rank r's heads are r*Hq/N .. (r+1)*Hq/N - 1).
+    global head order (rank r's heads are r*Hq/N .. (r+1)*Hq/N - 1).  ``out=``
+    takes that [B, Hq, q, D] result, as ``FusedHeadGather`` does.
     """
 
     group: dist.ProcessGroup | None = None
@@ -72,6 +73,7 @@ class HeadShardedDecode:
         fn = self.decode_fn
         if fn is None:
             from .paged_attention import paged_attention_decode as fn
+        dest = kw.pop("out", None)
         local = fn(query, key_cache, value_cache, block_tables, context_lens, scale, slot_mapping,
                    key, value, **kw)
         world = dist.get_world_size(self.group)
@@ -81,7 +83,13 @@ class HeadShardedDecode:
                 or self._gather_buf.dtype != local.dtype or self._gather_buf.device != local.device:
             self._gather_buf = torch.empty(shape, dtype=local.dtype, device=local.device)
         dist.all_gather_into_tensor(self._gather_buf, local.contiguous(), group=self.group)
-        return self._gather_buf.view(world, B, hl, q, D).permute(1, 0, 2, 3, 4).reshape(B, world * hl, q, D)
+        result = self._gather_buf.view(world, B, hl, q, D).permute(1, 0, 2, 3, 4)
+        if dest is None:
+            return result.reshape(B, world * hl, q, D)
+        if tuple(dest.shape) != (B, world * hl, q, D):
+            raise ValueError("out must be [batch, total query heads, q_len, head_dim]")
+        dest.view(B, world, hl, q, D).copy_(result)
+        return dest
 
 
 # Peer allocations mapped into this process, by IPC handle: an allocation is
@@ -131,6 +139,13 @@ class FusedHeadGather:
     rank that does not arrive in time is reported as
     ``PA_DEVERR_WAIT_TIMEOUT`` (``read_device_errors``) instead of hanging.
 
+    After a wait runs out the ranks no longer agree on which call is which, so
+    the kernel poisons the exchange: every later call on every rank reports
+    ``PA_DEVERR_GATHER``, and the call after one whose error has come back
+    raises RuntimeError.  A call that raised marks this object broken: it then
+    refuses calls until every rank has called ``close()``, and the next call
+    sets up fresh buffers and flags on every rank together.
+
     The gathered outputs are two buffers used in turn: another rank may start
     writing this rank's buffer for call k+2 as soon as this rank's kernel of
     call k+1 is done, so the tensor returned must be consumed by work ordered
@@ -145,14 +160,23 @@ class FusedHeadGather:
         self.wait_ns = int(wait_s * 1e9)
         self._state: _GatherState | None = None
         self._calls = 0
+        self._broken: str | None = None
         self._unfused = HeadShardedDecode(group=group)  # fp32: the kernel fuses fp16 / bf16 only
 
     def close(self) -> None:
         """Release the peer mappings and buffers (collective: every rank calls it
         after its last call; a barrier makes sure no rank still writes)."""
+        was_broken, self._broken = self._broken is not None, None
         if self._state is None:
             return
-        torch.cuda.synchronize(self._state.blob.device)
+        device = self._state.blob.device
+        torch.cuda.synchronize(device)
+        if was_broken:
+            # the poisoned calls' bits: reported already, and the flags they
+            # describe go away with this state
+            from .paged_attention import read_device_errors
+
+            read_device_errors(device, clear=True)
         dist.barrier(group=self.group)
         for hb in self._state.peer_handles:
             _ipc_drop(hb)
@@ -192,6 +216,9 @@ class FusedHeadGather:
             res = self._unfused(query, key_cache, value_cache, block_tables, context_lens, scale,
                                 slot_mapping, key, value, **kw)
             return res if dest is None else dest.copy_(res)
+        if self._broken is not None:
+            raise RuntimeError(f"fused gather out of step ({self._broken}): call close() on every rank, "
+                               "then start again")
         world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
         B, hl, q, D = query.shape
         key_ = (B, hl * world, q, D, query.dtype, query.device)
@@ -214,13 +241,17 @@ class FusedHeadGather:
         g.total_heads = hl * world
         dest = kw.pop("out", None)
         gathered = st.outs[par]
-        paged_attention_decode(query, key_cache, value_cache, block_tables, context_lens, scale, slot_mapping,
-                               key, value, out=gathered, gather=g, **kw)
+        try:
+            paged_attention_decode(query, key_cache, value_cache, block_tables, context_lens, scale, slot_mapping,
+                                   key, value, out=gathered, gather=g, **kw)
+        except Exception as exc:
+            # this rank's call did not run, or an earlier one failed: either way
+            # the ranks' calls no longer pair up
+            self._broken = f"{type(exc).__name__}: {exc}"
+            raise
         if dest is None:
             return gathered
         if tuple(dest.shape) != tuple(gathered.shape):
-            # HeadShardedDecode's out is the local [B, Hq/N, q, D] block; the
-            # gathered result needs a [B, Hq, q, D] destination
             raise ValueError("out must be [batch, total query heads, q_len, head_dim]")
         dest.copy_(gathered)
         return dest

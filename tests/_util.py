@@ -67,3 +67,42 @@ def excess_err(out: torch.Tensor, ref_f32: torch.Tensor) -> float:
     if out.dtype != torch.float32:
         bar = torch.maximum(bar, ulp(rr, out.dtype) * 1.0001)
     return (err - bar).max().item()
+
+
+def split_row_pieces(context_lens, q_len: int, G: int, Hkv: int, *, nw_total: int = 148 * 8,
+                     row_cost: int = 1, min_units: int = 8) -> dict[int, int]:
+    """Pieces the decode kernel's stream-K split cuts each sequence's rows into.
+
+    Replays the cost split of csrc/pa_decode_mma.cu: the flat order is sequence,
+    kv head, 16-row group; a row (b, h, mg) holds the 16-token units its last
+    query row attends and costs them plus ``row_cost`` (kRowCostUnitsPlain);
+    warp w owns the cost positions [C*w/nw, C*(w+1)/nw).  Returns, per sequence
+    b, the largest number of warps any of its rows spans (1 = never cut).
+    """
+    lens = [int(x) + q_len for x in torch.as_tensor(context_lens).cpu().tolist()]
+    GQ = G * q_len
+    NMG = (GQ + 15) // 16
+    rows = []  # (b, cost of unit 0, units)
+    cost = 0
+    for b, L in enumerate(lens):
+        for _h in range(Hkv):
+            for mg in range(NMG):
+                last_row = min(16 * mg + 15, GQ - 1)
+                lim = L - q_len + last_row // G
+                n = 0 if lim < 0 else (lim + 16) // 16
+                if n > 0:
+                    rows.append((b, cost + row_cost, n))
+                    cost += n + row_cost
+    C = cost
+    if C == 0:
+        return {}
+    nw = min(nw_total, max(1, (C + min_units - 1) // min_units))
+
+    def warp_at(x):
+        return ((x + 1) * nw - 1) // C
+
+    pieces: dict[int, int] = {}
+    for b, c0, n in rows:
+        k = warp_at(c0 + n - 1) - warp_at(c0) + 1
+        pieces[b] = max(pieces.get(b, 1), k)
+    return pieces

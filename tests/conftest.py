@@ -62,9 +62,10 @@ def _files(name: str) -> list[str]:
 
 
 def reference_root() -> Path | None:
-    """The reference checkout named by LLM_SERVING_RUNTIME_ROOT, when it exists."""
-    root = os.environ.get("LLM_SERVING_RUNTIME_ROOT")
-    if not root:
-        return None
-    p = Path(root)
-    return p if (p / "runtime" / "phase2" / "paged_attention_triton.py").exists() else None
+    """Where the reference's Python runtime can be imported from: the checkout
+    named by LLM_SERVING_RUNTIME_ROOT, else the unmodified copy that build()
+    stages in baseline/_ref (it travels with the working tree)."""
+    for root in (os.environ.get("LLM_SERVING_RUNTIME_ROOT"), str(REPO / "baseline" / "_ref")):
+        if root and (Path(root) / "runtime" / "phase2" / "paged_attention_triton.py").exists():
+            return Path(root)
+    return None

@@ -34,6 +34,17 @@ def test_library_exports_every_declared_symbol():
     assert exported == _declared_functions()
 
 
+def test_header_constants_match_the_binding():
+    text = HEADER.read_text()
+    defines = dict(re.findall(r"#define (PA_DEVERR_\w+) (0x[0-9a-fA-F]+)u", text))
+    assert defines, "no PA_DEVERR_ bits found"
+    for name, value in defines.items():
+        assert getattr(_lib, name) == int(value, 16), name
+    statuses = dict(re.findall(r"(PA_(?:OK|ERR_\w+)) = (\d+)", text))
+    for name, value in statuses.items():
+        assert getattr(_lib, name) == int(value), name
+
+
 def test_version():
     assert _lib.load().pa_version() == 10000
 

@@ -6,9 +6,9 @@ from __future__ import annotations
 import pytest
 import torch
 
+from _pool import LayeredKV
 from conftest import load_golden
 from llm_serving_runtime_b200 import kv_append, read_device_errors
-from llm_serving_runtime_b200.kv_block_pool import GpuKVBlockPool
 from llm_serving_runtime_b200.workloads import make_workload
 from oracle import oracle
 
@@ -35,31 +35,33 @@ def test_write_tokens_batch_matches_reference_bits(case, pos_dtype):
 
 
 @pytest.mark.parametrize("case", ["append_fp16", "append_bf16"])
-def test_pool_mirror_write_tokens_batch(case):
+def test_pool_write_tokens_batch_into_matches_reference_bits(case):
+    """kv_block_pool.write_tokens_batch_into on a 5-D layered pool, against the
+    reference's own write_tokens_batch outputs; the reference's underrun error."""
     data, meta = load_golden(case)
     kp0 = data["k_pool_before"]
     nb, L, Hkv, bs, D = kp0.shape
-    pool = GpuKVBlockPool(num_blocks=nb, block_size_tokens=bs, num_layers=L, num_kv_heads=Hkv, head_dim=D,
-                          dtype=kp0.dtype, device=DEV)
-    pool._grow_pools(nb)
-    pool._k_pool.copy_(kp0.to(DEV))
-    pool._v_pool.copy_(data["v_pool_before"].to(DEV))
+    pool = LayeredKV(nb, L, Hkv, bs, D, kp0.dtype, DEV)
+    pool.k.copy_(kp0.to(DEV))
+    pool.v.copy_(data["v_pool_before"].to(DEV))
     pool.write_tokens_batch(meta["layer_idx"], data["block_tables"], data["start_positions"],
                             data["key_states"].to(DEV), data["value_states"].to(DEV))
-    assert torch.equal(_bits(pool._k_pool), _bits(data["k_pool_after"]))
-    assert torch.equal(_bits(pool._v_pool), _bits(data["v_pool_after"]))
+    assert torch.equal(_bits(pool.k), _bits(data["k_pool_after"]))
+    assert torch.equal(_bits(pool.v), _bits(data["v_pool_after"]))
     with pytest.raises(IndexError, match="underrun"):
         pool.write_tokens_batch(0, data["block_tables"], torch.tensor([2, 7, 14]),
                                 data["key_states"].to(DEV), data["value_states"].to(DEV))
 
 
 def test_roundtrip_reference_test():
-    # tests/test_paged_kv_kernel.py:11-28 on the GPU pool
+    # tests/test_paged_kv_kernel.py:11-28 on a GPU pool: write two tokens of a
+    # single sequence through blocks [0, 1], read them back through the table
     data, _ = load_golden("roundtrip_fp32")
-    pool = GpuKVBlockPool(num_blocks=4, block_size_tokens=2, num_layers=1, num_kv_heads=2, head_dim=4,
-                          dtype=torch.float32, device=DEV)
-    pool.write_tokens(0, [0, 1], 0, data["key_states"].to(DEV), data["value_states"].to(DEV))
-    keys, values = pool.gather_layer(0, [0, 1], 2)
+    pool = LayeredKV(4, 1, 2, 2, 4, torch.float32, DEV)
+    pool.write_tokens_batch(0, torch.tensor([[0, 1]]), torch.tensor([0]), data["key_states"].to(DEV),
+                            data["value_states"].to(DEV))
+    keys = pool.k_layer_view(0)[:2].permute(1, 0, 2, 3).reshape(2, 4, 4)[:, :2].unsqueeze(0)
+    values = pool.v_layer_view(0)[:2].permute(1, 0, 2, 3).reshape(2, 4, 4)[:, :2].unsqueeze(0)
     assert keys.shape == (1, 2, 2, 4)
     assert torch.equal(keys.cpu(), data["keys"]) and torch.equal(values.cpu(), data["values"])
 

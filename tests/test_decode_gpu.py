@@ -12,9 +12,9 @@ import math
 import pytest
 import torch
 
-from _util import TOL, excess_err, max_err, oracle_rows
+from _util import TOL, excess_err, max_err, oracle_rows, split_row_pieces
 from conftest import decode_cases, load_golden
-from llm_serving_runtime_b200 import paged_attention_decode, read_device_errors
+from llm_serving_runtime_b200 import kv_append, paged_attention_decode, read_device_errors
 from llm_serving_runtime_b200.workloads import make_workload
 from oracle import oracle
 
@@ -64,24 +64,16 @@ def test_config1_append_and_decode_bit_exact_append():
     assert max_err(out, data["expected_torch"]) <= TOL[torch.float32]
 
 
-def _config_parity(name, rows_sample=None, seed_rows=0):
+def _config_parity(name, rows=None):
     w = make_workload(name, device=DEV)
     out = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens,
                                  w.scale, w.slot_mapping, w.new_key, w.new_value, validate=True)
     torch.cuda.synchronize()
-    B = w.batch
-    if rows_sample is None:
-        rows = list(range(B))
-    else:
-        g = torch.Generator().manual_seed(seed_rows)
-        rows = sorted(torch.randperm(B, generator=g)[:rows_sample].tolist())
-        # always include the longest and the shortest row
-        L = w.context_lens.cpu()
-        rows = sorted(set(rows) | {int(L.argmax()), int(L.argmin())})
+    rows = list(range(w.batch)) if rows is None else rows(w)
     ref = oracle_rows(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
                       w.q_len, rows)
     err = max_err(out[rows], ref)
-    assert err <= TOL[w.spec.dtype], f"{name}: max abs err {err}"
+    assert err <= TOL[w.spec.dtype], f"{name}: max abs err {err} over {len(rows)} rows"
     return w, out
 
 
@@ -89,18 +81,69 @@ def test_config2_qwen2_full_batch():
     _config_parity("cfg2-qwen2-0.5b")
 
 
-def test_config3_llama3_8b_sampled_rows():
-    _config_parity("cfg3-llama3-8b", rows_sample=40)
+def test_config3_llama3_8b_full_batch():
+    # all 256 rows; nearly every one is cut by a warp-slice boundary of the
+    # stream-K split and merged from up to 3 pieces
+    _config_parity("cfg3-llama3-8b")
 
 
-def test_config4_prefix_shared_verify_q4():
-    _config_parity("cfg4-prefix-verify", rows_sample=24)
+def test_config4_prefix_shared_verify_q4_full_batch():
+    _config_parity("cfg4-prefix-verify")
 
 
-def test_config5_llama3_70b_sampled_rows():
-    w, out = _config_parity("cfg5-llama3-70b", rows_sample=6)
+def _config5_rows(w, sample=64, seed=0):
+    """Rows the split cuts (a random 64 of them, with the most-cut first), every
+    row it does not cut, and the longest and shortest rows."""
+    s = w.spec
+    pieces = split_row_pieces(w.context_lens, s.q_len, s.num_q_heads // s.num_kv_heads, s.num_kv_heads)
+    cut = sorted(b for b, k in pieces.items() if k > 1)
+    whole = sorted(set(range(w.batch)) - set(cut))
+    g = torch.Generator().manual_seed(seed)
+    most = max(cut, key=lambda b: pieces[b])
+    picked = [cut[i] for i in torch.randperm(len(cut), generator=g)[:sample].tolist()]
+    L = w.context_lens.cpu()
+    rows = set(picked) | set(whole) | {most, int(L.argmax()), int(L.argmin())}
+    assert len(rows & set(cut)) >= sample
+    return sorted(rows)
+
+
+def test_config5_llama3_70b_rows_cut_by_the_split():
+    w, out = _config_parity("cfg5-llama3-70b", rows=_config5_rows)
     del w, out
     torch.cuda.empty_cache()
+
+
+def _append_touched_blocks_bit_exact(name):
+    """The step's append at full size, checked bit for bit on every block the
+    step's slots touch (a compact CPU copy through the oracle's scatter), and
+    every other block unchanged."""
+    w = make_workload(name, device=DEV)
+    bs = w.key_cache.shape[2]
+    slots = w.slot_mapping.cpu()
+    blocks = torch.unique(slots // bs)
+    index = torch.full((w.key_cache.shape[0],), -1, dtype=torch.int64)
+    index[blocks] = torch.arange(blocks.numel())
+    compact_slots = index[slots // bs] * bs + slots % bs
+    kc_ref, vc_ref = w.key_cache[blocks.to(DEV)].cpu(), w.value_cache[blocks.to(DEV)].cpu()
+    oracle.kv_append(w.new_key.cpu(), w.new_value.cpu(), kc_ref, vc_ref, compact_slots)
+    k_before, v_before = w.key_cache.clone(), w.value_cache.clone()
+    kv_append(w.new_key, w.new_value, w.key_cache, w.value_cache, w.slot_mapping, validate=True)
+    torch.cuda.synchronize()
+    bits = lambda t: t.contiguous().view(torch.int16)
+    assert torch.equal(bits(w.key_cache[blocks.to(DEV)].cpu()), bits(kc_ref))
+    assert torch.equal(bits(w.value_cache[blocks.to(DEV)].cpu()), bits(vc_ref))
+    # the rest of the pool: equal once the touched blocks are carried over
+    k_before[blocks.to(DEV)] = w.key_cache[blocks.to(DEV)]
+    v_before[blocks.to(DEV)] = w.value_cache[blocks.to(DEV)]
+    assert torch.equal(bits(w.key_cache), bits(k_before))
+    assert torch.equal(bits(w.value_cache), bits(v_before))
+    del w, k_before, v_before
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("name", ["cfg3-llama3-8b", "cfg5-llama3-70b"])
+def test_append_at_full_size_bit_exact(name):
+    _append_touched_blocks_bit_exact(name)
 
 
 def _synthetic(B, Hq, Hkv, D, bs, dtype, lens, q_len=1, seed=0, pool_extra=5, scale_v=0.5):

@@ -62,6 +62,9 @@ def test_one_rank_gather_equals_plain_decode():
         assert counters.tolist() == [call, 0] and flags.tolist() == [call]
 
 
+_POISONED_1 = (1 | 0x80000000) - (1 << 32)  # epoch 1 with the poison bit, read back as int32
+
+
 def test_missing_rank_times_out_without_a_fault():
     w = _workload(batch=24)
     plain = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)
@@ -74,13 +77,55 @@ def test_missing_rank_times_out_without_a_fault():
     paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
                            out=outs[0], gather=g)
     torch.cuda.synchronize()
-    assert read_device_errors(DEV) & DeviceErrorFlags.WAIT_TIMEOUT
+    assert read_device_errors(DEV) == DeviceErrorFlags.WAIT_TIMEOUT | DeviceErrorFlags.GATHER
     for o in outs:  # rank 0's rows reached both gathered outputs
         assert torch.equal(o[:, :Hq], plain)
-    assert flags[1].tolist() == [1, 0] and flags[0].tolist() == [1, 0]
+    # the wait ran out, so rank 0 poisoned its epoch and its flag at both ranks
+    assert flags[1].tolist() == [_POISONED_1, 0] and flags[0].tolist() == [_POISONED_1, 0]
+    assert counters.tolist() == [_POISONED_1, 0]
+    # the next gather call reports the broken exchange at once instead of waiting again
+    flags[1][1] = 2  # even a late flag of rank 1 does not revive it
+    paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                           out=outs[0], gather=g)
+    torch.cuda.synchronize()
+    assert read_device_errors(DEV) == DeviceErrorFlags.GATHER
+    assert counters.tolist() == [_POISONED_1, 0]
     again = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
                                    validate=True)
     assert torch.equal(again, plain)
+
+
+def test_peer_more_than_one_call_ahead_is_out_of_step():
+    w = _workload(batch=16)
+    plain = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)
+    B, Hq, q, D = plain.shape
+    outs = [torch.zeros(B, 2 * Hq, q, D, dtype=plain.dtype, device=DEV) for _ in range(2)]
+    flags = [torch.zeros(2, dtype=torch.int32, device=DEV) for _ in range(2)]
+    flags[0][1] = 3  # rank 1's flag claims it finished call 3 while rank 0 makes call 1
+    counters = torch.zeros(2, dtype=torch.int32, device=DEV)
+    g = _args(outs, flags, counters, 0, 0, 2 * Hq, 2_000_000_000)
+    read_device_errors(DEV)
+    paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                           out=outs[0], gather=g)
+    torch.cuda.synchronize()
+    assert read_device_errors(DEV) == DeviceErrorFlags.GATHER
+    assert counters.tolist() == [_POISONED_1, 0]
+
+
+def test_bad_block_id_raises_at_the_next_call_without_validate():
+    w = _workload(batch=8)
+    args = (w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)
+    read_device_errors(DEV)
+    bad = w.block_tables.clone()
+    bad[3, 0] = w.key_cache.shape[0] + 7
+    paged_attention_decode(w.query, w.key_cache, w.value_cache, bad, w.context_lens, w.scale)  # returns
+    torch.cuda.synchronize()  # the error word's copy has landed
+    with pytest.raises(IndexError, match="out of range"):
+        paged_attention_decode(*args)
+    assert read_device_errors(DEV) == 0  # raising read and cleared it
+    good = paged_attention_decode(*args)
+    torch.cuda.synchronize()
+    assert torch.equal(paged_attention_decode(*args), good)
 
 
 def _free_port() -> int:
@@ -115,16 +160,36 @@ def _two_rank_worker(rank: int, port: int) -> None:
         torch.cuda.synchronize()
         dist.barrier()
         fused.close()
-        # failure detection: rank 1 skips one call, rank 0 reports the timeout
+        # failure detection: rank 1 skips one call, rank 0's wait runs out
         short = FusedHeadGather(wait_s=0.2)
         short(*args)
         torch.cuda.synchronize()
         dist.barrier()
-        read_device_errors(dev)
+        assert read_device_errors(dev, clear=False) == 0
         if rank == 0:
             short(*args)
             torch.cuda.synchronize()
-            assert read_device_errors(dev) & DeviceErrorFlags.WAIT_TIMEOUT
+        dist.barrier()
+        # the call after the skip reports the failure on both ranks instead of
+        # returning rows of different calls: rank 0 raises on the error that came
+        # back; rank 1's kernel finds rank 0's poisoned flag, and its next call raises
+        if rank == 0:
+            with pytest.raises(RuntimeError, match="timed out"):
+                short(*args)
+        else:
+            short(*args)
+            torch.cuda.synchronize()
+            with pytest.raises(RuntimeError, match="out of step"):
+                short(*args)
+        with pytest.raises(RuntimeError, match="close"):
+            short(*args)  # broken until every rank closes
+        dist.barrier()
+        short.close()
+        # a fresh set-up on both ranks pairs the calls up again
+        for _ in range(2):
+            assert torch.equal(short(*args), nccl(*args))
+        torch.cuda.synchronize()
+        assert read_device_errors(dev) == 0
         dist.barrier()
         short.close()
     finally:

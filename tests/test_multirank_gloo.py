@@ -78,9 +78,14 @@ def _head_worker(rank, world, port, out_q):
     kc = w.key_cache[:, h0:h0 + hc].clone()
     vc = w.value_cache[:, h0:h0 + hc].clone()
     q = w.query[:, h0 * G:(h0 + hc) * G].contiguous()
-    out = HeadShardedDecode(decode_fn=_oracle_decode)(
-        q, kc, vc, w.block_tables, w.context_lens, w.scale, w.slot_mapping,
-        w.new_key[:, h0:h0 + hc].contiguous(), w.new_value[:, h0:h0 + hc].contiguous())
+    args = (q, kc, vc, w.block_tables, w.context_lens, w.scale, w.slot_mapping,
+            w.new_key[:, h0:h0 + hc].contiguous(), w.new_value[:, h0:h0 + hc].contiguous())
+    out = HeadShardedDecode(decode_fn=_oracle_decode)(*args)
+    # out= receives the gathered [B, Hq, q, D] result, as the fused form does
+    dest = torch.empty_like(out)
+    kc.copy_(w.key_cache[:, h0:h0 + hc])
+    vc.copy_(w.value_cache[:, h0:h0 + hc])
+    assert HeadShardedDecode(decode_fn=_oracle_decode)(*args, out=dest) is dest and torch.equal(dest, out)
     if rank == 0:
         out_q.put(out.float().numpy())  # by value: the worker exits right after
     dist.destroy_process_group()

@@ -1,6 +1,7 @@
-"""The drop-in modules on the GPU: the reference's own parity tests replayed
-through reference_api / kv_block_pool, the HF hook, and the batched cache flow
-(append -> metadata -> hook) the reference's BlockPagedBatchLayer.update drives."""
+"""The reference-API shim on the GPU: the reference's own parity tests replayed
+through reference_api over a layered test pool whose append is
+kv_block_pool.write_tokens_batch_into.  (The reference's own cache, hook and
+graph manager on top of the kernels are in test_reference_runtime_gpu.py.)"""
 
 from __future__ import annotations
 
@@ -9,30 +10,43 @@ import math
 import pytest
 import torch
 
+from _pool import LayeredKV
 from _util import excess_err
 from llm_serving_runtime_b200 import reference_api as ra
-from llm_serving_runtime_b200.block_paged_attention import block_paged_attention_forward
-from llm_serving_runtime_b200.kv_block_pool import GpuKVBlockPool
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
+def _write_seq(pool, layer, block_ids, k, v):
+    """One sequence's tokens 0..n-1 through its blocks (the reference's write_tokens)."""
+    pool.write_tokens_batch(layer, torch.tensor([block_ids]), torch.tensor([0]), k, v)
+
+
+def _gather(pool, layer, block_ids, seq_len):
+    """Dense [1, kv_heads, seq_len, dim] K/V of one sequence (the reference's gather_layer)."""
+    n = math.ceil(seq_len / pool.block_size_tokens)
+    ids = torch.tensor(block_ids[:n], device=pool.device)
+    k = pool.k_layer_view(layer)[ids].permute(1, 0, 2, 3)
+    v = pool.v_layer_view(layer)[ids].permute(1, 0, 2, 3)
+    H, D = k.shape[0], k.shape[-1]
+    return k.reshape(H, -1, D)[:, :seq_len].unsqueeze(0), v.reshape(H, -1, D)[:, :seq_len].unsqueeze(0)
+
+
 def _run_parity(*, dtype, num_kv_heads, num_kv_groups, head_dim, block_size, seq_len):
     """tests/test_paged_attention_kernel_parity.py:19-79 with the CUDA branch."""
     num_heads = num_kv_heads * num_kv_groups
     num_blocks = math.ceil(seq_len / block_size) + 1
-    pool = GpuKVBlockPool(num_blocks=num_blocks, block_size_tokens=block_size, num_layers=1,
-                          num_kv_heads=num_kv_heads, head_dim=head_dim, dtype=dtype, device=DEV)
+    pool = LayeredKV(num_blocks, 1, num_kv_heads, block_size, head_dim, dtype, DEV)
     block_ids = list(range(num_blocks))
     torch.manual_seed(42)
     k = torch.randn(1, num_kv_heads, seq_len, head_dim, device=DEV, dtype=dtype)
     v = torch.randn(1, num_kv_heads, seq_len, head_dim, device=DEV, dtype=dtype)
-    pool.write_tokens(0, block_ids, 0, k, v)
+    _write_seq(pool, 0, block_ids, k, v)
     query = torch.randn(1, num_heads, 1, head_dim, device=DEV, dtype=dtype)
     scaling = head_dim ** -0.5
-    keys, values = pool.gather_layer(0, block_ids, seq_len)
+    keys, values = _gather(pool, 0, block_ids, seq_len)
     expected = ra.reference_sdpa_attention(query, keys, values, scaling, num_kv_groups)
     actual = ra.paged_attention_decode(query=query, pool=pool, layer_idx=0, block_ids=block_ids,
                                        seq_len=seq_len, num_kv_groups=num_kv_groups, scaling=scaling)
@@ -62,8 +76,7 @@ def test_batched_ragged_reference_test():
     dtype, num_kv_heads, num_kv_groups, head_dim, block_size = torch.float16, 2, 4, 64, 16
     batch_size, seq_lens = 4, [7, 15, 31, 63]
     num_blocks = math.ceil(max(seq_lens) / block_size) + 2
-    pool = GpuKVBlockPool(num_blocks=num_blocks * batch_size, block_size_tokens=block_size, num_layers=1,
-                          num_kv_heads=num_kv_heads, head_dim=head_dim, dtype=dtype, device=DEV)
+    pool = LayeredKV(num_blocks * batch_size, 1, num_kv_heads, block_size, head_dim, dtype, DEV)
     torch.manual_seed(99)
     scaling = head_dim ** -0.5
     num_heads = num_kv_heads * num_kv_groups
@@ -76,7 +89,7 @@ def test_batched_ragged_reference_test():
         block_tables[b, :nlog] = torch.tensor(ids[:nlog], device=DEV, dtype=torch.int32)
         k = torch.randn(1, num_kv_heads, sl, head_dim, device=DEV, dtype=dtype)
         v = torch.randn(1, num_kv_heads, sl, head_dim, device=DEV, dtype=dtype)
-        pool.write_tokens(0, ids, 0, k, v)
+        _write_seq(pool, 0, ids, k, v)
         rows.append((ids, sl))
     query = torch.randn(batch_size, num_heads, 1, head_dim, device=DEV, dtype=dtype)
     meta = ra.PagedDecodeBatchMetadata(pool=pool, layer_idx=0, block_tables=block_tables,
@@ -84,14 +97,13 @@ def test_batched_ragged_reference_test():
     actual = ra.paged_attention_decode_batched(query, meta, num_kv_groups, scaling)
     for b, (ids, sl) in enumerate(rows):
         nlog = math.ceil(sl / block_size)
-        keys, values = pool.gather_layer(0, ids[:nlog], sl)
+        keys, values = _gather(pool, 0, ids[:nlog], sl)
         expected = ra.reference_sdpa_attention(query[b:b + 1], keys, values, scaling, num_kv_groups)
         assert (expected - actual[b:b + 1]).abs().max().item() < 1e-2
 
 
 def test_q_len_other_than_one_rejected_like_the_reference():
-    pool = GpuKVBlockPool(num_blocks=4, block_size_tokens=16, num_layers=1, num_kv_heads=2, head_dim=64,
-                          dtype=torch.float16, device=DEV)
+    pool = LayeredKV(4, 1, 2, 16, 64, torch.float16, DEV)
     q = torch.zeros(1, 8, 2, 64, device=DEV, dtype=torch.float16)
     meta = ra.PagedDecodeBatchMetadata(pool, 0, torch.zeros(1, 2, dtype=torch.int32, device=DEV),
                                        torch.tensor([5], dtype=torch.int32, device=DEV))
@@ -101,45 +113,9 @@ def test_q_len_other_than_one_rejected_like_the_reference():
         ra.paged_attention_decode(q[:, :, :1], pool, 0, [0], 0, 4, 0.125)
 
 
-def test_hook_and_batched_cache_flow():
-    """What BlockPagedBatchLayer.update + the attention hook do per layer
-    (paged_kv_cache.py:136-166, block_paged_attention.py:35-48)."""
-    B, Hkv, G, D, bs, layers = 5, 8, 4, 128, 16, 2
-    g = torch.Generator().manual_seed(0)
-    ctx = torch.tensor([3, 16, 100, 250, 31])
-    max_blocks = 20
-    pool = GpuKVBlockPool(num_blocks=B * max_blocks, block_size_tokens=bs, num_layers=layers,
-                          num_kv_heads=Hkv, head_dim=D, dtype=torch.bfloat16, device=DEV)
-    pool.reserve()
-    pool._k_pool.copy_((torch.randn(pool._k_pool.shape, generator=g) * 0.5).to(torch.bfloat16))
-    pool._v_pool.copy_((torch.randn(pool._v_pool.shape, generator=g) * 0.5).to(torch.bfloat16))
-    tables = torch.randperm(B * max_blocks, generator=g).reshape(B, max_blocks).to(torch.int32).to(DEV)
-    seq_lens = ctx.to(torch.int32).to(DEV)
-
-    class Attn:
-        num_key_value_groups = G
-        training = False
-
-    for layer in range(layers):
-        k_new = (torch.randn(B, Hkv, 1, D, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
-        v_new = (torch.randn(B, Hkv, 1, D, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
-        q = (torch.randn(B, Hkv * G, 1, D, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
-        pool.write_tokens_batch(layer, tables, seq_lens, k_new, v_new)
-        meta = ra.PagedDecodeBatchMetadata(pool=pool, layer_idx=layer, block_tables=tables, seq_lens=seq_lens + 1)
-        token = ra.set_paged_decode_batch_metadata(meta)
-        out, weights = block_paged_attention_forward(Attn(), q, k_new, v_new, None, D ** -0.5)
-        ra.reset_paged_decode_batch_metadata(token)
-        assert weights is None and out.shape == (B, 1, Hkv * G, D)
-        ref = oracle.paged_decode(q.cpu(), pool.k_layer_view(layer).cpu(), pool.v_layer_view(layer).cpu(),
-                                  tables.cpu(), seq_lens.cpu() + 1, D ** -0.5, len_offset=0)
-        assert excess_err(out.transpose(1, 2), ref) <= 0
-    assert pool.allocated_block_count() > 0
-
-
 def test_triton_available_and_warmup():
     assert ra.triton_available()
-    pool = GpuKVBlockPool(num_blocks=4, block_size_tokens=16, num_layers=1, num_kv_heads=2, head_dim=128,
-                          dtype=torch.bfloat16, device=DEV)
+    pool = LayeredKV(4, 1, 2, 16, 128, torch.bfloat16, DEV)
     ra.warmup_paged_attention_kernel(pool, num_heads=8, num_kv_groups=4, head_dim=128, block_ids=[0, 1])
 
 
@@ -151,15 +127,14 @@ def test_batched_speculative_verify_through_the_pool():
     cached = [5, 60, 333, 1000, 16]
     B = len(cached)
     nmax = math.ceil((max(cached) + k) / bs)
-    pool = GpuKVBlockPool(num_blocks=B * nmax + 1, block_size_tokens=bs, num_layers=2, num_kv_heads=Hkv,
-                          head_dim=D, dtype=dtype, device=DEV)
+    pool = LayeredKV(B * nmax + 1, 2, Hkv, bs, D, dtype, DEV)
     g = torch.Generator(device="cpu").manual_seed(7)
     perm = torch.randperm(B * nmax + 1, generator=g)[: B * nmax].view(B, nmax).to(torch.int32)
     tables = perm.to(DEV)
     for b, c in enumerate(cached):  # the cached context of each row, layer 1
         kk = torch.randn(1, Hkv, c, D, generator=g).to(dtype).to(DEV)
         vv = torch.randn(1, Hkv, c, D, generator=g).to(dtype).to(DEV)
-        pool.write_tokens(1, perm[b].tolist(), 0, kk, vv)
+        _write_seq(pool, 1, perm[b].tolist(), kk, vv)
     new_k = torch.randn(B, Hkv, k, D, generator=g).to(dtype).to(DEV)
     new_v = torch.randn(B, Hkv, k, D, generator=g).to(dtype).to(DEV)
     pool.write_tokens_batch(1, tables, torch.tensor(cached, device=DEV), new_k, new_v)

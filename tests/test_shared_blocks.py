@@ -18,7 +18,6 @@ from pathlib import Path
 import pytest
 import torch
 
-from llm_serving_runtime_b200.kv_block_pool import GpuKVBlockPool
 from llm_serving_runtime_b200.prefix_sharing import find_shared_prefixes
 from llm_serving_runtime_b200.shared_blocks import BlockRefAllocator
 
@@ -160,19 +159,22 @@ def test_copy_on_write_copies_only_the_shared_block_written():
 
 def test_copy_on_write_moves_the_pool_contents():
     torch.manual_seed(0)
-    pool = GpuKVBlockPool(num_blocks=12, block_size_tokens=4, num_layers=2, num_kv_heads=2, head_dim=8,
-                          dtype=torch.float32, device="cpu")
-    pool.reserve()
-    pool._k_pool.copy_(torch.randn_like(pool._k_pool))
-    pool._v_pool.copy_(torch.randn_like(pool._v_pool))
-    k_before, v_before = pool._k_pool.clone(), pool._v_pool.clone()
+    k_pool = torch.randn(12, 2, 2, 4, 8)  # [blocks, layers, kv heads, block size, head dim]
+    v_pool = torch.randn(12, 2, 2, 4, 8)
+
+    def copy_blocks(src_ids, dst_ids):
+        for s, d in zip(src_ids, dst_ids):
+            k_pool[d] = k_pool[s]
+            v_pool[d] = v_pool[s]
+
+    k_before, v_before = k_pool.clone(), v_pool.clone()
     alloc = BlockRefAllocator(total_blocks=12, block_size_tokens=4)
     a = alloc.allocate_for_tokens("a", 8)
     entry = alloc.snapshot_blocks(a.block_ids)
     b = alloc.allocate_for_tokens("b", 12, borrowed_block_ids=entry)
-    (old, new), = alloc.make_writable("b", 6, 1, pool.copy_blocks)
-    assert torch.equal(pool._k_pool[new], k_before[old]) and torch.equal(pool._v_pool[new], v_before[old])
-    assert torch.equal(pool._k_pool[old], k_before[old])  # the shared original is untouched
+    (old, new), = alloc.make_writable("b", 6, 1, copy_blocks)
+    assert torch.equal(k_pool[new], k_before[old]) and torch.equal(v_pool[new], v_before[old])
+    assert torch.equal(k_pool[old], k_before[old])  # the shared original is untouched
     assert b.block_ids[1] == new
 
 

@@ -12,9 +12,9 @@ from __future__ import annotations
 import pytest
 import torch
 
+from _pool import LayeredKV
 from _util import excess_err, max_err
 from llm_serving_runtime_b200 import find_shared_prefixes, paged_attention_decode
-from llm_serving_runtime_b200.kv_block_pool import GpuKVBlockPool
 from llm_serving_runtime_b200.shared_blocks import BlockRefAllocator
 from oracle import oracle
 
@@ -24,9 +24,7 @@ DEV = torch.device("cuda", 0)
 
 def test_borrowed_prefix_blocks_through_the_cascade():
     bs, Hkv, Hq, D, dtype, layer = 16, 2, 16, 128, torch.bfloat16, 1
-    pool = GpuKVBlockPool(num_blocks=96, block_size_tokens=bs, num_layers=2, num_kv_heads=Hkv, head_dim=D,
-                          dtype=dtype, device=DEV)
-    pool.reserve()
+    pool = LayeredKV(96, 2, Hkv, bs, D, dtype, DEV)
     alloc = BlockRefAllocator(total_blocks=96, block_size_tokens=bs)
     g = torch.Generator().manual_seed(11)
 

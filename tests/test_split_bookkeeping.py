@@ -21,7 +21,17 @@ import random
 import pytest
 
 
-ROW_COST = 2  # kRowCostUnits in csrc/pa_internal.h
+def _header_constant(name: str) -> int:
+    import re
+    from pathlib import Path
+
+    text = (Path(__file__).resolve().parent.parent / "llm_serving_runtime_b200" / "csrc" / "pa_internal.h").read_text()
+    return int(re.search(rf"constexpr int {name} = (\d+);", text).group(1))
+
+
+# The row costs the kernel uses (plain decode and the cascade's suffix pass).
+ROW_COST = _header_constant("kRowCostUnitsPlain")
+ROW_COST_CASCADE = _header_constant("kRowCostUnitsCascade")
 
 
 def _warp_of(x, nw, C):
@@ -114,7 +124,7 @@ def _decode_rows(rng, B, Hkv, groups):
 
 
 @pytest.mark.parametrize("seed", range(6))
-@pytest.mark.parametrize("row_cost", [ROW_COST, 0, 5])
+@pytest.mark.parametrize("row_cost", [ROW_COST, ROW_COST_CASCADE, 0, 5])
 def test_split_bookkeeping_invariants(seed, row_cost):
     rng = random.Random(seed)
     for _ in range(150):

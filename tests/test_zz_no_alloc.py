@@ -3,9 +3,14 @@ allocate device memory (a plugin host that passes only inputs and outputs, a
 serving loop whose free HBM all belongs to the KV pool).  Its scratch is a
 fixed array inside the library, so it takes no workspace argument.
 
-Called through the C ABI (ctypes) and compared with the regular entry point
-pa_decode (caller-provided workspace) on two calls in a row with different
-inputs, so scratch left by the first call must not leak into the second.
+Called through the C ABI (ctypes).  Each call is compared with the regular
+entry point pa_decode (caller-provided workspace), which launches the same
+deterministic kernel, so the two must agree bit for bit; one call is also
+checked against the CPU oracle.  The calls come in a row with different
+shapes and dtypes, so scratch left by one call must not leak into the next.
+After its first call on a device the entry point needs no free device memory
+at all: a call made with all but a sliver of HBM handed to a stand-in KV pool
+must succeed and leave the free memory unchanged.
 Collected last on purpose; it also passes alone in a fresh process.
 """
 
@@ -16,7 +21,7 @@ import ctypes
 import pytest
 import torch
 
-from _util import TOL, max_err
+from _util import TOL, max_err, oracle_rows
 from llm_serving_runtime_b200 import _lib, paged_attention_decode
 from llm_serving_runtime_b200.workloads import make_workload
 
@@ -53,8 +58,8 @@ def _args(w, out) -> _lib.DecodeArgs:
     return a
 
 
-def _static_decode(w) -> torch.Tensor:
-    out = torch.empty_like(w.query)
+def _static_decode(w, out=None) -> torch.Tensor:
+    out = torch.empty_like(w.query) if out is None else out
     args = _args(w, out)
     stream = torch.cuda.current_stream(DEV).cuda_stream
     rc = _lib.load().pa_decode_static_workspace(ctypes.byref(args), stream)
@@ -62,17 +67,59 @@ def _static_decode(w) -> torch.Tensor:
     return out
 
 
-def test_static_workspace_matches_pa_decode_on_two_calls_in_a_row():
+def _expected(w):
+    return paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)
+
+
+def test_static_workspace_equals_pa_decode_on_calls_in_a_row():
     torch.cuda.set_device(DEV)
-    first = make_workload("cfg3-llama3-8b", device=DEV, rows=list(range(48)))
-    second = make_workload("cfg5-llama3-70b", device=DEV, rows=list(range(24)))
-    for w in (first, second):
-        expected = paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables,
-                                          w.context_lens, w.scale)
+    cases = [
+        make_workload("cfg3-llama3-8b", device=DEV, rows=list(range(48))),   # bf16, rows cut by the split
+        make_workload("cfg5-llama3-70b", device=DEV, rows=list(range(24))),  # bf16, G = 8
+        make_workload("cfg2-qwen2-0.5b", device=DEV),                        # fp16, D = 64
+        make_workload("cfg1-fp32-small", device=DEV),                        # fp32 kernel
+        make_workload("cfg3-llama3-8b", device=DEV, rows=list(range(100, 148))),
+    ]
+    for w in cases:
+        expected = _expected(w)
         got = _static_decode(w)
         torch.cuda.synchronize()
-        err = max_err(got, expected.float())
-        assert err <= TOL[w.query.dtype], f"{w.spec.name}: max abs err {err}"
+        assert torch.equal(got, expected), f"{w.spec.name}: differs from pa_decode"
+
+
+def test_static_workspace_against_the_oracle():
+    torch.cuda.set_device(DEV)
+    w = make_workload("cfg2-qwen2-0.5b", device=DEV)
+    got = _static_decode(w)
+    torch.cuda.synchronize()
+    rows = list(range(w.batch))
+    ref = oracle_rows(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale, w.q_len, rows)
+    assert max_err(got, ref) <= TOL[w.query.dtype]
+
+
+def test_static_workspace_needs_no_free_memory_after_its_first_call():
+    torch.cuda.set_device(DEV)
+    w = make_workload("cfg3-llama3-8b", device=DEV, rows=list(range(32)))
+    expected = _expected(w)
+    out = torch.empty_like(w.query)
+    _static_decode(w, out)  # first call on this device: the library's device code and array are set up
+    torch.cuda.synchronize()
+    free, _ = torch.cuda.mem_get_info(DEV)
+    margin = 256 << 20
+    pool_stand_in = torch.empty(max(0, free - margin), dtype=torch.uint8, device=DEV) if free > margin else None
+    try:
+        out.zero_()
+        torch.cuda.synchronize()
+        before, _ = torch.cuda.mem_get_info(DEV)
+        for _ in range(2):
+            _static_decode(w, out)
+            torch.cuda.synchronize()
+            assert torch.equal(out, expected)
+        after, _ = torch.cuda.mem_get_info(DEV)
+        assert after == before, f"free device memory changed by {before - after} bytes"
+    finally:
+        del pool_stand_in
+        torch.cuda.empty_cache()
 
 
 def test_static_workspace_rejects_shapes_beyond_its_size():

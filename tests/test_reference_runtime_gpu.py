@@ -268,9 +268,10 @@ def test_single_sequence_layer_prefill_and_decode(ref):
 
 def _graph_manager_run(root: str) -> dict:
     """The reference's CudaGraphDecodeManager over a small random Llama: three
-    requests prefilled one at a time (as the worker does), bound to a
-    persistent batch, then decode steps through try_decode; each step is also
-    run as the manager's own eager step on a twin pool."""
+    requests prefilled one at a time (as the worker does, through the
+    multi-query path), bound to a persistent batch, then decode steps through
+    try_decode; each step is also run as the manager's own eager step on a
+    twin pool."""
     import os
 
     os.environ["PHASE2_CUDA_GRAPH"] = "1"
@@ -285,7 +286,24 @@ def _graph_manager_run(root: str) -> dict:
     integration.install()
     torch.manual_seed(0)
     cfg = _config(2, 16, 4, 128, vocab=512)
-    model = LlamaForCausalLM(cfg).to(device=DEV, dtype=BF16).eval()
+    llama = LlamaForCausalLM(cfg).to(device=DEV, dtype=BF16).eval()
+
+    class PositionsFromCachePosition(torch.nn.Module):
+        """The manager hands the model each row's position as cache_position
+        (cuda_graph_decode.py:119, :180-186).  transformers 5.5's Llama ignores
+        it and derives position ids from the cache-level get_seq_length(),
+        whose .item() (paged_kv_cache.py:407) invalidates any capture; this
+        wrapper passes the manager's positions as position ids instead."""
+
+        def __init__(self, inner):
+            super().__init__()
+            self.inner = inner
+
+        def forward(self, input_ids, past_key_values, cache_position=None, use_cache=True):
+            return self.inner(input_ids=input_ids, past_key_values=past_key_values,
+                              position_ids=cache_position.view(-1, 1), use_cache=use_cache)
+
+    model = PositionsFromCachePosition(llama)
     prompts = [torch.randint(0, 512, (1, n)) for n in (23, 57, 130)]
 
     def setup():
@@ -298,7 +316,7 @@ def _graph_manager_run(root: str) -> dict:
             for i, ids in enumerate(prompts):
                 cache = mods.paged_kv_cache.BlockPagedCache(cfg, pool)
                 cache.set_block_ids(list(range(16 * i + 1, 16 * i + 13)))
-                model(input_ids=ids.to(DEV), past_key_values=cache, use_cache=True)
+                llama(input_ids=ids.to(DEV), past_key_values=cache, use_cache=True)
                 state = SimpleNamespace(req=SimpleNamespace(request_id=f"r{i}"), past_key_values=cache)
                 persistent.bind_cache(f"r{i}", cache)
                 states.append(state)

@@ -333,6 +333,94 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_multi_token_compare(args) -> None:
+    """One multi-token layer step through the reference's own cache layer and
+    attention hook (BlockPagedBatchLayer.update, paged_kv_cache.py:121-170;
+    block_paged_attention_forward, block_paged_attention.py:24-59) on the
+    ``prefill-llama3-8b`` shapes: stock (its per-token append loop, the dense
+    gather and eager attention, on the GPU) against integration.install()
+    (append kernel, then the multi-query kernels over the paged cache), and the
+    stock attention after the installed append (gather + eager alone).  Device
+    time per step with CUDA events; one JSON line."""
+    from llm_serving_runtime_b200 import integration
+    from llm_serving_runtime_b200.workloads import SPECS, attention_flops, make_workload
+
+    root = None
+    for cand in (os.environ.get("LLM_SERVING_RUNTIME_ROOT"), str(REPO / "baseline" / "_ref")):
+        if cand and (Path(cand) / "runtime" / "phase2" / "paged_kv_cache.py").exists():
+            root = cand
+            break
+    if root is None:
+        print(json.dumps({"multi_token_compare": "unavailable: reference runtime not importable"}))
+        return
+    sys.path.insert(0, root)
+    import runtime.phase2.block_paged_attention as bpa
+    import runtime.phase2.paged_kv_cache as pkc
+    import runtime.phase2.paged_kv_kernel as pkk
+    from transformers import LlamaConfig
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    spec = SPECS["prefill-llama3-8b"]
+    w = make_workload(spec, device=dev)
+    B, Hq, q, D = w.query.shape
+    Hkv, bs = spec.num_kv_heads, spec.block_size
+    nb = w.key_cache.shape[0]
+    cfg = LlamaConfig(hidden_size=Hq * D, num_hidden_layers=1, num_attention_heads=Hq, num_key_value_heads=Hkv,
+                      head_dim=D, intermediate_size=256, vocab_size=256)
+    pool = pkk.GpuKVBlockPool(num_blocks=nb, block_size_tokens=bs, num_layers=1, num_kv_heads=Hkv, head_dim=D,
+                              dtype=w.query.dtype, device=dev)
+    pool._grow_pools(nb)
+    pool._k_pool[:, 0].copy_(w.key_cache)
+    pool._v_pool[:, 0].copy_(w.value_cache)
+    cache = pkc.BlockPagedBatchCache(cfg, pool, block_tables=w.block_tables, seq_lens=w.context_lens,
+                                     block_ids_rows=[[] for _ in range(B)])
+    layer = cache.layers[0]
+    start = w.context_lens.clone()
+
+    class Attn:
+        num_key_value_groups = Hq // Hkv
+        training = False
+        is_causal = True
+
+    def step():
+        layer._row_seq_lens = start.clone()
+        cache.seq_lens = start.clone()
+        k, v = layer.update(w.new_key, w.new_value)
+        return bpa.block_paged_attention_forward(Attn(), w.query, k, v, None, w.scale)[0]
+
+    def timed(fn, n):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    n = max(3, min(args.steps, 20))
+    stock_ms = timed(step, n)
+    integration.install(multi_query=False)  # the append kernel, the reference's gather + eager attention
+    append_only_ms = timed(step, n)
+    integration.uninstall()
+    integration.install()
+    installed_ms = timed(step, n)
+    integration.uninstall()
+    print(json.dumps({
+        "multi_token_compare": spec.name, "batch": B, "q_len": q, "num_q_heads": Hq, "num_kv_heads": Hkv,
+        "head_dim": D, "context_lens": f"{spec.length_dist} [{spec.length_lo}, {spec.length_hi}]",
+        "steps": n, "ms_stock_reference": stock_ms, "ms_installed_append_stock_attention": append_only_ms,
+        "ms_installed": installed_ms, "speedup_vs_stock": stock_ms / installed_ms,
+        "speedup_vs_gather_eager": append_only_ms / installed_ms,
+        "attention_tflops_installed": attention_flops(w) / (installed_ms / 1e3) / 1e12,
+        "note": "the stock eager hook receives no mask (None) from this call, so it attends every gathered "
+                "position; the installed path attends causally over the new tokens",
+    }), flush=True)
+
+
 def _shard_mode(args, world: int) -> str:
     """Multi-GPU layout: KV heads for config 5 at N > 1 (auto), sequences otherwise."""
     if args.shard != "auto":
@@ -347,6 +435,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="cfg3-llama3-8b")
+    ap.add_argument("--multi-token-compare", action="store_true",
+                    help="time a prefill layer step through the reference's cache and hook, stock vs installed")
     ap.add_argument("--no-kvhead-record", action="store_true",
                     help="skip the config-5 KV-head-sharding record added to every other workload's line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -367,6 +457,9 @@ def main() -> None:
 
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.multi_token_compare:
+        run_multi_token_compare(args)
         return
 
     import torch.distributed as dist

@@ -505,6 +505,14 @@ def main() -> None:
         raise SystemExit("--prefix-sharing on needs a workload with shared prefixes on the sequence-sharded path")
     graph = None
     if args.graph:
+        # eager calls first: the per-SM shares learn from them, and the graph
+        # then keeps the shares it was captured with
+        from llm_serving_runtime_b200.paged_attention import SmSpeeds
+
+        for _ in range(2 * SmSpeeds.SAMPLES):
+            paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale,
+                                   out=out, prefix_groups=pg)
+            torch.cuda.synchronize()
         if gather is not None:
             raise SystemExit("--graph covers the single-rank and sequence-sharded steps")
         from llm_serving_runtime_b200.cuda_graph import DecodeStepGraph
@@ -534,6 +542,15 @@ def main() -> None:
         if world > 1:
             dist.barrier()
 
+    # Untimed: the per-SM shares learn from the first large calls (each call's
+    # timing records come back before the next one); a fixed number of calls,
+    # so every rank makes the same calls.
+    from llm_serving_runtime_b200.paged_attention import SmSpeeds
+
+    share_calls = 0 if graph is not None else 2 * SmSpeeds.SAMPLES
+    for _ in range(share_calls):
+        step()
+        torch.cuda.synchronize()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -674,6 +691,7 @@ def main() -> None:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "overlap": "2 copy streams, double-buffered", "result_matches_device_run": ok},
         "gpu_launches": gpu_launches,
+        "sm_shares": dict(_sm_shares_summary(dev), untimed_learning_calls=2 * SmSpeeds.SAMPLES),
         "ms_per_step_by_rank": [round(v, 5) for v in rank_ms],
         "kernel_ms_by_rank": [round(v, 5) for v in dec_ms_by_rank],
         "clocks": clk,
@@ -683,6 +701,16 @@ def main() -> None:
     if kvhead is not None:
         line["kvhead_shard"] = kvhead
     print(json.dumps(line), flush=True)
+
+
+def _sm_shares_summary(dev) -> dict:
+    """The per-SM share weights of the large decode calls (paged_attention.SmSpeeds)."""
+    from llm_serving_runtime_b200.paged_attention import _SM_SHARES, sm_speeds
+
+    t = sm_speeds(dev)
+    w = t.weights[: t.n] if t.n else t.weights
+    return {"on": bool(_SM_SHARES and t.n), "samples": t.samples, "learning": t.learning,
+            "min": round(float(w.min()), 4), "max": round(float(w.max()), 4)}
 
 
 def _e2e_measure(dev, stream, inputs: dict, call, out_shape, out_dtype, download: bool, n: int, barrier,

@@ -134,7 +134,29 @@ typedef struct pa_decode_args {
   size_t workspace_bytes;
   int32_t allow_overlap_with_previous; /* 1: programmatic dependent launch on the kernel
                                           launched just before on `stream` (pa_kv_append) */
+  /* Per-SM shares of large fp16/bf16 decode calls (no counterpart in the
+   * reference; NULL / 0: equal shares).  sm_weights is host memory, one
+   * relative speed per SM of the device (num_sm_weights = its SM count); it is
+   * read at the call, so a launch (or a captured graph) keeps the shares it was
+   * given.  A call whose work gives every warp at least 64 units (16 tokens of
+   * one KV head) splits its cost in proportion to them, SM by SM.  With
+   * sm_timing_tag != 0 such a call also writes one pa_sm_timing record per SM
+   * at PA_WS_SM_TIMING_OFFSET in the workspace, tagged with it, so the caller
+   * can derive the speeds (see paged_attention.py). */
+  const float* sm_weights;
+  int32_t num_sm_weights;
+  uint32_t sm_timing_tag;
 } pa_decode_args;
+
+/* One SM's share of a large decode call: when it started and finished (the
+ * GPU's global timer, ns), the cost units it held (16-token units plus a
+ * fixed cost per row), the SM it ran on and the call's tag. */
+typedef struct pa_sm_timing {
+  uint64_t t_start_ns, t_end_ns;
+  uint32_t cost, smid, tag, pad;
+} pa_sm_timing;
+#define PA_WS_SM_TIMING_OFFSET 256
+#define PA_MAX_SM_WEIGHTS 160
 
 /* Scatter new K/V rows into the paged cache.  Bit-exact copy.
  * Replaces: GpuKVBlockPool.write_tokens_batch, runtime/phase2/paged_kv_kernel.py:176-227

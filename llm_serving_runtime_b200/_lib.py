@@ -105,7 +105,27 @@ class DecodeArgs(ctypes.Structure):
         ("workspace", _vp),
         ("workspace_bytes", _sz),
         ("allow_overlap_with_previous", _i32),
+        ("sm_weights", _vp),
+        ("num_sm_weights", _i32),
+        ("sm_timing_tag", ctypes.c_uint32),
     ]
+
+
+class SmTiming(ctypes.Structure):
+    """pa_sm_timing: one SM's share of a large decode call."""
+
+    _fields_ = [
+        ("t_start_ns", ctypes.c_uint64),
+        ("t_end_ns", ctypes.c_uint64),
+        ("cost", ctypes.c_uint32),
+        ("smid", ctypes.c_uint32),
+        ("tag", ctypes.c_uint32),
+        ("pad", ctypes.c_uint32),
+    ]
+
+
+PA_WS_SM_TIMING_OFFSET = 256
+PA_MAX_SM_WEIGHTS = 160
 
 
 class PrefixGroupsArgs(ctypes.Structure):

@@ -187,7 +187,32 @@ DecodeShape decode_shape(int Hq, int Hkv, int q_len) {
 // slots].  The counters sit at a fixed offset whatever the call's shape, so a
 // workspace shared by calls of different shapes keeps them at zero.
 size_t workspace_bytes_impl(int slot_rows, int D, int nw_total) {
-  return pa::kWsHeaderBytes + pa::ws_counter_bytes(nw_total) + pa::ws_partial_bytes(nw_total, slot_rows, D);
+  return pa::kWsFixedBytes + pa::ws_counter_bytes(nw_total) + pa::ws_partial_bytes(nw_total, slot_rows, D);
+}
+
+// Fixed-point cumulative shares of the SMs from host weights; false (equal
+// shares) when the weights do not describe this device or are not usable.
+static_assert(sizeof(pa::SlotTiming) == sizeof(pa_sm_timing), "timing record layout");
+static_assert(pa::kWsHeaderBytes == PA_WS_SM_TIMING_OFFSET, "timing record offset");
+static_assert(pa::kMaxSlots == PA_MAX_SM_WEIGHTS, "SM weight count");
+static_assert((pa::kMaxSlots + 1) * 4 <= (int)pa::kWsClaimBytes, "slot claim words");
+
+bool slot_fractions(const float* w, int n, int num_sms, uint32_t* frac) {
+  if (w == nullptr || n != num_sms || n <= 0 || n > pa::kMaxSlots) return false;
+  double tot = 0.0;
+  for (int i = 0; i < n; ++i) {
+    if (!(w[i] > 0.f) || !(w[i] < 1e30f)) return false;
+    tot += w[i];
+  }
+  const double one = (double)(1u << pa::kSlotFracBits);
+  double run = 0.0;
+  frac[0] = 0;
+  for (int i = 0; i < n; ++i) {
+    run += w[i];
+    frac[i + 1] = i + 1 == n ? (1u << pa::kSlotFracBits) : (uint32_t)(run / tot * one + 0.5);
+    if (frac[i + 1] <= frac[i]) return false;  // every share must be non-empty
+  }
+  return true;
 }
 
 // Cascade prefix pass: how many token ranges (splits) each group's prefix is
@@ -547,8 +572,14 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, con
   if (a->workspace_bytes < need)
     return fail(PA_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", a->workspace_bytes, need);
   char* ws = static_cast<char*>(a->workspace);
-  p.counters = reinterpret_cast<int32_t*>(ws + pa::kWsHeaderBytes);
-  p.partials = reinterpret_cast<float*>(ws + pa::kWsHeaderBytes + pa::ws_counter_bytes(p.nw_total));
+  p.slot_timing = reinterpret_cast<pa::SlotTiming*>(ws + pa::kWsHeaderBytes);
+  p.slot_claims = reinterpret_cast<int32_t*>(ws + pa::kWsHeaderBytes + pa::kWsTimingBytes);
+  p.counters = reinterpret_cast<int32_t*>(ws + pa::kWsFixedBytes);
+  p.partials = reinterpret_cast<float*>(ws + pa::kWsFixedBytes + pa::ws_counter_bytes(p.nw_total));
+  if (slot_fractions(a->sm_weights, a->num_sm_weights, info->num_sms, p.slot_frac)) {
+    p.n_slots = info->num_sms;
+    p.timing_tag = a->sm_timing_tag;
+  }
   if (gat != nullptr) {
     p.out_ranks = gat->out_ranks;
     p.flags_ranks = gat->flags_ranks;
@@ -575,7 +606,7 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, con
   }
 
   // Ring depth: as many 16-token stages per warp as shared memory allows (2..8).
-  const size_t budget = (size_t)info->max_smem_optin - 64;  // static shared memory of the kernel
+  const size_t budget = (size_t)info->max_smem_optin - 128;  // static shared memory of the kernel (96 B)
   int stages = 8;
   while (stages >= 2 && pa::decode_mma_smem_bytes(D, p.B, stages, cascade) > budget) --stages;
   if (stages < 2)

@@ -212,6 +212,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
+// The SM this thread runs on.
+__device__ __forceinline__ uint32_t smid_u32() {
+  uint32_t v;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(v));
+  return v;
+}
 // Nanoseconds of the GPU's global timer.
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;

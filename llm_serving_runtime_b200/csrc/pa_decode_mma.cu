@@ -322,7 +322,92 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   long long nw_eff = (C + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
   if (nw_eff > p.nw_total) nw_eff = p.nw_total;
   if (nw_eff < 1) nw_eff = 1;
-  const int gw = blockIdx.x * kDecodeWarps + warp;
+  // Per-SM shares.  SMs stream at different speeds (up to ~10 % apart, in a
+  // pattern fixed by where they sit), so with equal shares the call ends with
+  // the slowest SMs.  Large calls given per-SM weights (p.n_slots, one slot per
+  // SM) instead cut the cost line into one share per slot in proportion to
+  // its SM's measured speed, and each CTA takes the slot of the SM it runs on
+  // (or, should that one be taken, the first free one: the grid has one CTA
+  // per slot, so every slot is taken exactly once).  The 8 warps of a slot
+  // split it equally.  Which CTA runs a slot does not change the numbers:
+  // shares, pieces and merges follow the slots.
+  const bool weighted = p.n_slots > 0 && p.n_slots == (int)gridDim.x &&
+                        nw_eff == (long long)p.n_slots * kDecodeWarps &&
+                        C >= nw_eff * (long long)kWeightedMinUnitsPerWarp;
+  __shared__ int s_slot;
+  __shared__ unsigned long long s_t0, s_t1;
+  __shared__ int s_warps_out;
+  if (weighted) {
+    if (tid == 0) {
+      const int smid = (int)smid_u32();
+      int sl = -1;
+      if (smid < p.n_slots && atomicCAS(&p.slot_claims[smid], 0, 1) == 0) sl = smid;
+      for (int i = 0; sl < 0 && i < p.n_slots; ++i)
+        if (atomicCAS(&p.slot_claims[i], 0, 1) == 0) sl = i;
+      s_slot = sl;
+      s_t0 = ~0ull;
+      s_t1 = 0ull;
+      s_warps_out = 0;
+    }
+    __syncthreads();
+  }
+  const int gw = weighted ? s_slot * kDecodeWarps + warp : blockIdx.x * kDecodeWarps + warp;
+  // Cost at which slot s starts (s = n_slots: C).
+  auto slot_bound = [&](int sl) -> long long { return (C * (long long)p.slot_frac[sl]) >> kSlotFracBits; };
+  // Cost at which global warp g's share starts (g = nw_eff: C).
+  auto warp_start = [&](int g) -> long long {
+    if (!weighted) return C * g / nw_eff;
+    const int sl = g / kDecodeWarps, w = g - sl * kDecodeWarps;
+    const long long b0 = slot_bound(sl);
+    return w == 0 ? b0 : b0 + (slot_bound(sl + 1) - b0) * w / kDecodeWarps;
+  };
+  // The global warp whose share holds cost position x (0 <= x < C).
+  auto warp_at_cost = [&](long long x) -> int {
+    if (!weighted) return (int)(((x + 1) * nw_eff - 1) / C);
+    int lo = 0, hi = p.n_slots - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (slot_bound(mid) <= x)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    const long long b0 = slot_bound(lo), len = slot_bound(lo + 1) - b0;
+    return lo * kDecodeWarps + (int)(((x - b0 + 1) * kDecodeWarps - 1) / len);
+  };
+  // Every warp of a weighted call counts itself out once: the CTA's last one
+  // writes the slot's timing record (when asked), and the grid's last one
+  // clears the slot claims for the next call.
+  auto leave_weighted = [&]() {
+    if (!weighted) return;
+    __syncwarp();
+    if (lane == 0) {
+      const unsigned long long t = (unsigned long long)global_ns();
+      atomicMax(&s_t1, t);
+      __threadfence_block();
+      if (atomicAdd(&s_warps_out, 1) == kDecodeWarps - 1 && p.timing_tag != 0u && s_slot >= 0) {
+        __threadfence_block();
+        SlotTiming* r = p.slot_timing + s_slot;
+        r->t_start_ns = s_t0;
+        r->t_end_ns = s_t1;
+        r->cost = (uint32_t)(slot_bound(s_slot + 1) - slot_bound(s_slot));
+        r->smid = smid_u32();
+        r->tag = p.timing_tag;
+      }
+      int32_t* done = p.slot_claims + kMaxSlots;
+      if (atomicAdd(done, 1) == (int)gridDim.x * kDecodeWarps - 1) {
+        for (int i = 0; i < p.n_slots; ++i) p.slot_claims[i] = 0;
+        *done = 0;
+      }
+    }
+  };
+  if (weighted && s_slot < 0) {  // cannot happen (one CTA per slot); leave the work undone and say so
+    if (lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
+    leave_weighted();
+    finish_warp();
+    return;
+  }
+  if (weighted && lane == 0) atomicMin(&s_t0, (unsigned long long)global_ns());
   auto cost_pref = [&](int b) -> long long { return (long long)s_pref[b] + (long long)kRowCostUnits * s_rpref[b]; };
   // Cost at which row group mg of kv head h of sequence b starts.
   auto row_cost_start = [&](int b, int h, int mg) -> long long {
@@ -363,11 +448,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     }
     return f;
   };
-  // The warp whose cost share holds position x.
-  auto warp_at_cost = [&](long long x) -> int { return (int)(((x + 1) * nw_eff - 1) / C); };
-  const long long ws = unit_at_cost(C * gw / nw_eff);
-  const long long we = unit_at_cost(C * (gw + 1) / nw_eff);
+  const long long ws = unit_at_cost(warp_start(gw));
+  const long long we = unit_at_cost(warp_start(gw + 1));
   if (gw >= nw_eff || ws >= we) {
+    leave_weighted();
     finish_warp();
     return;
   }
@@ -574,6 +658,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         mbar_wait_bounded(my_bars + (uint32_t)s * 8u, (phase >> s) & 1u);
         s = (s + 1 == stages) ? 0 : s + 1;
       }
+      leave_weighted();
       finish_warp();
       return;
     }
@@ -671,7 +756,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         if (old == npieces - 1) {
           // Last arrival: log-sum-exp merge of all pieces of this row.
           __threadfence();
-          const bool gw1_first = unit_at_cost(C * gw1 / nw_eff) == row_start;
+          const bool gw1_first = unit_at_cost(warp_start(gw1)) == row_start;
           auto slot_ptr = [&](int i) -> const float* {
             const int g2 = gw1 + i;
             const int si = (i == 0 && !gw1_first) ? 2 * g2 + 1 : 2 * g2;
@@ -828,6 +913,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     ++cf;
     slot = (slot + 1 == stages) ? 0 : slot + 1;
   }
+  leave_weighted();
   finish_warp();
 }
 

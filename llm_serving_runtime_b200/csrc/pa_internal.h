@@ -33,8 +33,23 @@ constexpr int kRowCostUnitsCascade = 4;
 // Split rows of at most this many pieces are merged in the MMA fragment layout
 // (all loads in flight at once); longer ones by the lane-parallel merge.
 constexpr int kFragMergePieces = 4;
-// Layout of the workspace: status word, then merge counters, then partial slots.
+// Layout of the workspace: status word (header), per-SM timing records and
+// slot claims, then merge counters, then partial slots.
 constexpr size_t kWsHeaderBytes = 256;
+// Per-SM shares of the decode kernel's cost line (large calls): at most this
+// many SMs, fixed-point cumulative fractions with kSlotFracBits bits, used when
+// every warp's share holds at least kWeightedMinUnitsPerWarp units of cost.
+constexpr int kMaxSlots = 160;
+constexpr int kSlotFracBits = 20;
+constexpr int kWeightedMinUnitsPerWarp = 64;
+// One timing record per slot (pa_sm_timing in the public header).
+struct SlotTiming {
+  unsigned long long t_start_ns, t_end_ns;
+  uint32_t cost, smid, tag, pad;
+};
+constexpr size_t kWsTimingBytes = kMaxSlots * sizeof(SlotTiming);
+constexpr size_t kWsClaimBytes = 1024;  // kMaxSlots claim words + the done counter, rounded
+constexpr size_t kWsFixedBytes = kWsHeaderBytes + kWsTimingBytes + kWsClaimBytes;
 
 // Kernel-side description of one decode call (passed by value).
 struct DecodeParams {
@@ -61,6 +76,13 @@ struct DecodeParams {
   float* partials;   // [2 * nw_total] slots of (m, l, O) partial states
   int32_t slot_rows; // rows stored per partial slot
   int32_t nw_total;  // warps in the grid
+  // Per-SM shares (n_slots > 0): slot s (taken by the CTA on SM s, or by any
+  // CTA whose SM's slot is taken) covers the cost [C*f[s], C*f[s+1]) >> 20.
+  int32_t n_slots;
+  uint32_t slot_frac[kMaxSlots + 1];
+  int32_t* slot_claims;      // [kMaxSlots] claim words, then the done counter (zero between calls)
+  SlotTiming* slot_timing;   // [n_slots] records, written when timing_tag != 0
+  uint32_t timing_tag;
   int32_t stages;    // shared-memory ring depth per warp
   // Shared prompt prefixes (pa_decode_cascade); seq_group is null otherwise.
   // The prefix kernel attends group g's member rows over tokens [0, P_g) with

@@ -95,8 +95,8 @@ extern "C" PA_API int pa_decode_static_workspace(const pa_decode_args* args, voi
     return pa::set_last_error(PA_ERR_WORKSPACE, msg);
   }
 
-  // Error word and merge counters must start at zero.
-  const size_t zero_bytes = pa::kWsHeaderBytes + pa::ws_counter_bytes(num_sms * pa::kDecodeWarps);
+  // Error word, slot claims and merge counters must start at zero.
+  const size_t zero_bytes = pa::kWsFixedBytes + pa::ws_counter_bytes(num_sms * pa::kDecodeWarps);
   e = cudaMemsetAsync(ws, 0, zero_bytes, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return pa::set_last_error(PA_ERR_CUDA, "cudaMemsetAsync(static workspace) failed");
 

@@ -48,6 +48,7 @@ import ctypes
 import os
 import threading
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -61,6 +62,8 @@ __all__ = [
     "describe_device_errors",
     "device_error",
     "DeviceErrorFlags",
+    "SmSpeeds",
+    "sm_speeds",
 ]
 
 _DTYPE_CODE = {
@@ -108,6 +111,9 @@ def describe_device_errors(flags: int) -> str:
 
 
 _VALIDATE_DEFAULT = os.environ.get("PA_B200_VALIDATE", "0") == "1"
+# Per-SM shares of large decode calls (SmSpeeds); PA_B200_SM_SHARES=0 keeps
+# every SM's share equal.
+_SM_SHARES = os.environ.get("PA_B200_SM_SHARES", "1") != "0"
 
 # One workspace per device: status word + merge counters + partial slots.
 _ws_lock = threading.Lock()
@@ -163,17 +169,116 @@ def read_device_errors(device: torch.device | None = None, *, clear: bool = True
     return int(flags.value)
 
 
-class _PendingCheck:
-    """One in-flight copy of a device error word into pinned host memory."""
+# The workspace's first bytes: the device error word at 0, then (at
+# PA_WS_SM_TIMING_OFFSET) one pa_sm_timing record per SM.
+_TIMING_DTYPE = np.dtype([("t0", "<u8"), ("t1", "<u8"), ("cost", "<u4"), ("smid", "<u4"), ("tag", "<u4"),
+                          ("pad", "<u4")])
+_HEAD_BYTES = _lib.PA_WS_SM_TIMING_OFFSET + _lib.PA_MAX_SM_WEIGHTS * _TIMING_DTYPE.itemsize
 
-    __slots__ = ("host", "stream", "after_call", "landed", "pending")
+
+class SmSpeeds:
+    """Relative streaming speed of each SM of one device.
+
+    The decode kernel gives every SM of a large call a share of the work in
+    proportion to these weights (pa_decode_args.sm_weights): SMs stream at
+    speeds up to ~10 % apart, in a pattern fixed by where they sit, and equal
+    shares would leave the call waiting on the slowest.  The weights start
+    equal.  The first SAMPLES large calls on the device each write one timing
+    record per SM (pa_sm_timing: its share and how long it took), which comes
+    back with the error word's asynchronous copy.  An SM's speed varies a
+    little from call to call (two calls' speeds correlate about 0.87 on B200),
+    so the weights are the mean of the relative speeds over the samples so far.
+    After SAMPLES samples they stay fixed, so later calls split their work
+    identically and give bit-identical results on identical inputs.  A call too
+    small for per-SM shares writes no records; after one, the next calls are
+    tagged only every 2, 4, ... 1024 calls, so small calls pay almost nothing."""
+
+    SAMPLES = 8
+
+    def __init__(self, num_sms: int):
+        self.n = num_sms if 0 < num_sms <= _lib.PA_MAX_SM_WEIGHTS else 0
+        self.weights = torch.ones(max(self.n, 1), dtype=torch.float32)  # host memory the C call reads
+        self.weights_ptr = self.weights.data_ptr()  # updated in place, so the address stays
+        self.samples = 0
+        self._tag = 0
+        self._sum = np.zeros(max(self.n, 1))
+        self._misses = 0
+        self._skip = 0
+
+    @property
+    def learning(self) -> bool:
+        return self.n > 0 and self.samples < self.SAMPLES
+
+    def want_sample(self) -> bool:
+        """Whether the next call should carry a tag (backs off after misses)."""
+        if not self.learning:
+            return False
+        if self._skip > 0:
+            self._skip -= 1
+            return False
+        return True
+
+    def new_tag(self) -> int:
+        self._tag = self._tag % 0x7FFFFFFF + 1
+        return self._tag
+
+    def absorb(self, tag: int, raw: np.ndarray) -> bool:
+        """Take one call's timing records (raw bytes); False when they are not
+        that call's (a call too small for per-SM shares writes none)."""
+        rec = raw.view(_TIMING_DTYPE)[: self.n]
+        if rec.shape[0] != self.n or (rec["tag"] != tag).any():
+            self._misses = min(self._misses + 1, 10)
+            self._skip = 1 << self._misses
+            return False
+        self._misses = 0
+        smid = rec["smid"].astype(np.int64)
+        if smid.max() >= self.n or np.unique(smid).size != self.n:
+            return False  # a CTA ran off its own SM: the records do not say which SM was how fast
+        busy = (rec["t1"].astype(np.int64) - rec["t0"].astype(np.int64)).astype(np.float64)
+        if (busy <= 0).any() or (rec["cost"] == 0).any():
+            return False
+        speed = rec["cost"].astype(np.float64) / busy
+        rel = np.empty(self.n)
+        rel[smid] = speed / speed.mean()
+        self._sum += np.clip(rel, 0.6, 1.6)
+        self.samples += 1
+        w = self._sum / self.samples
+        w = w / w.mean()
+        self.weights.copy_(torch.from_numpy(w.astype(np.float32)))
+        return True
+
+
+_speeds_lock = threading.Lock()
+_speeds: dict[int, SmSpeeds] = {}
+
+
+def sm_speeds(device: torch.device) -> SmSpeeds:
+    """The device's per-SM speed table (created on first use)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _speeds.get(idx)
+    if t is not None:
+        return t
+    with _speeds_lock:
+        t = _speeds.get(idx)
+        if t is None:
+            t = _speeds[idx] = SmSpeeds(torch.cuda.get_device_properties(idx).multi_processor_count)
+        return t
+
+
+class _PendingCheck:
+    """One in-flight copy of a workspace's first bytes (the device error word,
+    and after a tagged call the per-SM timing records) into pinned memory."""
+
+    __slots__ = ("host", "stream", "after_call", "landed", "pending", "tag", "speeds")
 
     def __init__(self, device: torch.device):
-        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.host = torch.zeros(_HEAD_BYTES, dtype=torch.uint8, pin_memory=True)
         self.stream = torch.cuda.Stream(device)
         self.after_call = torch.cuda.Event()
         self.landed = torch.cuda.Event()
         self.pending = False
+        self.tag = 0
+        self.speeds = None
 
 
 _checks_lock = threading.Lock()
@@ -192,17 +297,30 @@ def _raise_landed_errors(word: torch.Tensor) -> None:
         if c is None or not c.pending or not c.landed.query():
             return
         c.pending = False
-        seen = int(c.host.item())
+        seen = int(c.host[:4].view(torch.int32).item())
+        if c.tag:
+            n = c.speeds.n
+            c.speeds.absorb(c.tag, c.host.numpy()[_lib.PA_WS_SM_TIMING_OFFSET:][: n * _TIMING_DTYPE.itemsize])
+            c.tag = 0
     if seen:
         flags = seen | read_device_errors(workspace=word, clear=True)
         raise device_error(flags)
 
 
-def _copy_after_call(word: torch.Tensor, stream: torch.cuda.Stream) -> None:
+def _copy_is_free(word: torch.Tensor) -> bool:
+    """No copy of ``word``'s workspace is in flight (the next one may carry timing)."""
+    with _checks_lock:
+        c = _checks.get((word.device.index, word.data_ptr()))
+        return c is None or not c.pending
+
+
+def _copy_after_call(word: torch.Tensor, stream: torch.cuda.Stream, tag: int = 0,
+                     speeds: "SmSpeeds | None" = None) -> None:
     """Queue a copy of ``word`` to pinned host memory behind the work on
     ``stream`` (on a side stream, so ``stream`` is not held up).  While one copy
     is in flight no other is queued: the word keeps its bits until read, so the
-    next copy covers every call since."""
+    next copy covers every call since.  After a call tagged ``tag`` the copy
+    also takes the call's per-SM timing records, for ``speeds``."""
     key = (word.device.index, word.data_ptr())
     with _checks_lock:
         c = _checks.get(key)
@@ -214,8 +332,12 @@ def _copy_after_call(word: torch.Tensor, stream: torch.cuda.Stream) -> None:
             return
         c.after_call.record(stream)
         c.stream.wait_event(c.after_call)
+        nbytes = 4
+        if tag and speeds is not None and word.numel() >= _lib.PA_WS_SM_TIMING_OFFSET + speeds.n * 32:
+            nbytes = _lib.PA_WS_SM_TIMING_OFFSET + speeds.n * _TIMING_DTYPE.itemsize
+            c.tag, c.speeds = tag, speeds
         with torch.cuda.stream(c.stream):
-            c.host.copy_(word[:4].view(torch.int32), non_blocking=True)
+            c.host[:nbytes].copy_(word[:nbytes], non_blocking=True)
         word.record_stream(c.stream)  # a replaced workspace stays allocated until the copy has run
         c.landed.record(c.stream)
         c.pending = True
@@ -501,6 +623,15 @@ def paged_attention_decode(
     args.workspace = workspace.data_ptr()
     args.workspace_bytes = workspace.numel()
     args.allow_overlap_with_previous = 1 if appended else 0
+    speeds = sm_speeds(device)
+    tag = 0
+    if speeds.n and _SM_SHARES:
+        args.sm_weights = speeds.weights_ptr
+        args.num_sm_weights = speeds.n
+        if deferred and speeds.learning and query.dtype != torch.float32 and _copy_is_free(workspace) \
+                and speeds.want_sample():
+            tag = speeds.new_tag()
+            args.sm_timing_tag = tag
     with _with_device(device):
         if gather is not None:
             _lib.check(lib.pa_decode_gather(ctypes.byref(args), ctypes.byref(gather), _stream_ptr(device)),
@@ -512,7 +643,7 @@ def paged_attention_decode(
         else:
             _lib.check(lib.pa_decode(ctypes.byref(args), _stream_ptr(device)), "pa_decode")
     if deferred:
-        _copy_after_call(workspace, torch.cuda.current_stream(device))
+        _copy_after_call(workspace, torch.cuda.current_stream(device), tag, speeds)
     elif validate if validate is not None else _VALIDATE_DEFAULT:
         flags = read_device_errors(workspace=workspace)
         if flags:

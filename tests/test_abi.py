@@ -63,6 +63,9 @@ int main(void) {
   F(pa_decode_args, key_cache) F(pa_decode_args, block_tables) F(pa_decode_args, context_lens)
   F(pa_decode_args, out) F(pa_decode_args, batch) F(pa_decode_args, scale) F(pa_decode_args, workspace)
   F(pa_decode_args, workspace_bytes) F(pa_decode_args, allow_overlap_with_previous)
+  F(pa_decode_args, sm_weights) F(pa_decode_args, num_sm_weights) F(pa_decode_args, sm_timing_tag)
+  printf("pa_sm_timing %zu\n", sizeof(pa_sm_timing));
+  F(pa_sm_timing, cost) F(pa_sm_timing, tag)
   printf("pa_prefix_groups %zu\n", sizeof(pa_prefix_groups));
   F(pa_prefix_groups, max_prefix_len) F(pa_prefix_groups, member_offsets) F(pa_prefix_groups, seq_group)
   printf("pa_gather_args %zu\n", sizeof(pa_gather_args));
@@ -87,7 +90,9 @@ def test_ctypes_structs_match_header_layout(tmp_path):
     assert int(c["pa_prefix_groups"]) == ctypes.sizeof(_lib.PrefixGroupsArgs)
     assert int(c["pa_gather_args"]) == ctypes.sizeof(_lib.GatherArgs)
     assert int(c["pa_ipc_handle"]) == ctypes.sizeof(_lib.IpcHandle)
+    assert int(c["pa_sm_timing"]) == ctypes.sizeof(_lib.SmTiming)
     classes = {"pa_kv_append_args": _lib.KvAppendArgs, "pa_decode_args": _lib.DecodeArgs,
+               "pa_sm_timing": _lib.SmTiming,
                "pa_prefix_groups": _lib.PrefixGroupsArgs, "pa_gather_args": _lib.GatherArgs,
                "pa_ipc_handle": _lib.IpcHandle}
     for key, val in c.items():

@@ -23,6 +23,7 @@ import torch
 
 from _util import TOL, max_err, oracle_rows
 from llm_serving_runtime_b200 import _lib, paged_attention_decode
+from llm_serving_runtime_b200.paged_attention import sm_speeds
 from llm_serving_runtime_b200.workloads import make_workload
 
 pytestmark = pytest.mark.gpu
@@ -55,6 +56,12 @@ def _args(w, out) -> _lib.DecodeArgs:
     a.scale = w.scale
     a.workspace = None      # ignored by the static-workspace entry point
     a.workspace_bytes = 0
+    # the per-SM shares paged_attention_decode passes, so both entry points
+    # split large calls the same way
+    speeds = sm_speeds(DEV)
+    if speeds.n:
+        a.sm_weights = speeds.weights.data_ptr()
+        a.num_sm_weights = speeds.n
     return a
 
 

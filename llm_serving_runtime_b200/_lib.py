@@ -210,6 +210,35 @@ def load() -> ctypes.CDLL:
         return lib
 
 
+_cudart_handle: ctypes.CDLL | None = None
+_cudart_tried = False
+
+
+def cudart() -> ctypes.CDLL | None:
+    """The CUDA runtime this process already uses (libcudart.so.12), for the
+    few raw stream, event and copy calls of the host path (no torch wrapper
+    per call); None when it cannot be loaded."""
+    global _cudart_handle, _cudart_tried
+    with _lock:
+        if _cudart_tried:
+            return _cudart_handle
+        _cudart_tried = True
+        try:
+            rt = ctypes.CDLL("libcudart.so.12")
+        except OSError:
+            return None
+        rt.cudaEventCreateWithFlags.argtypes = [ctypes.POINTER(_vp), ctypes.c_uint]
+        rt.cudaEventRecord.argtypes = [_vp, _vp]
+        rt.cudaStreamWaitEvent.argtypes = [_vp, _vp, ctypes.c_uint]
+        rt.cudaMemcpyAsync.argtypes = [_vp, _vp, _sz, ctypes.c_int, _vp]
+        rt.cudaEventQuery.argtypes = [_vp]
+        for f in (rt.cudaEventCreateWithFlags, rt.cudaEventRecord, rt.cudaStreamWaitEvent, rt.cudaMemcpyAsync,
+                  rt.cudaEventQuery):
+            f.restype = ctypes.c_int
+        _cudart_handle = rt
+        return rt
+
+
 def last_error() -> str:
     msg = load().pa_last_error()
     return msg.decode() if msg else ""

@@ -121,7 +121,9 @@ _workspaces: dict[int, torch.Tensor] = {}
 
 
 def _stream_ptr(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The current stream's raw handle (no Stream object per call)."""
+    return torch._C._cuda_getCurrentRawStream(device.index if device.index is not None
+                                              else torch.cuda.current_device())
 
 
 def decode_workspace(device: torch.device, nbytes: int = 256) -> torch.Tensor:
@@ -267,18 +269,34 @@ def sm_speeds(device: torch.device) -> SmSpeeds:
 
 class _PendingCheck:
     """One in-flight copy of a workspace's first bytes (the device error word,
-    and after a tagged call the per-SM timing records) into pinned memory."""
+    and after a tagged call the per-SM timing records) into pinned memory.
 
-    __slots__ = ("host", "stream", "after_call", "landed", "pending", "tag", "speeds")
+    The copy runs on a side stream behind an event recorded on the call's
+    stream, through raw CUDA runtime calls on the handles (a few microseconds
+    of host time per call; torch's stream and event wrappers cost ten times
+    that).  The workspace tensor is held until the copy has landed, so the
+    caching allocator cannot hand its memory out meanwhile."""
 
-    def __init__(self, device: torch.device):
+    __slots__ = ("host", "host_ptr", "side", "side_ptr", "ev_call", "ev_landed", "pending", "tag", "speeds",
+                 "word")
+
+    def __init__(self, device: torch.device, rt):
         self.host = torch.zeros(_HEAD_BYTES, dtype=torch.uint8, pin_memory=True)
-        self.stream = torch.cuda.Stream(device)
-        self.after_call = torch.cuda.Event()
-        self.landed = torch.cuda.Event()
+        self.host_ptr = self.host.data_ptr()
+        with torch.cuda.device(device):
+            self.side = torch.cuda.Stream(device)
+            self.side_ptr = self.side.cuda_stream
+            evs = []
+            for _ in range(2):
+                ev = ctypes.c_void_p()
+                if rt.cudaEventCreateWithFlags(ctypes.byref(ev), 0x2) != 0:  # cudaEventDisableTiming
+                    raise RuntimeError("cudaEventCreateWithFlags failed")
+                evs.append(ev.value)
+        self.ev_call, self.ev_landed = evs
         self.pending = False
         self.tag = 0
         self.speeds = None
+        self.word = None
 
 
 _checks_lock = threading.Lock()
@@ -292,11 +310,19 @@ def _capturing() -> bool:
 def _raise_landed_errors(word: torch.Tensor) -> None:
     """Raise for the device errors of earlier calls on ``word`` whose copy has
     landed (the word is read again and cleared, synchronously, only then)."""
+    c = _checks.get((word.device.index, word.data_ptr()))
+    if c is None or not c.pending:
+        return
     with _checks_lock:
-        c = _checks.get((word.device.index, word.data_ptr()))
-        if c is None or not c.pending or not c.landed.query():
+        if not c.pending:
             return
+        q = _lib.cudart().cudaEventQuery(c.ev_landed)
+        if q == 600:  # cudaErrorNotReady
+            return
+        if q != 0:
+            raise RuntimeError(f"cudaEventQuery on the error-word copy failed ({q})")
         c.pending = False
+        c.word = None
         seen = int(c.host[:4].view(torch.int32).item())
         if c.tag:
             n = c.speeds.n
@@ -309,42 +335,44 @@ def _raise_landed_errors(word: torch.Tensor) -> None:
 
 def _copy_is_free(word: torch.Tensor) -> bool:
     """No copy of ``word``'s workspace is in flight (the next one may carry timing)."""
-    with _checks_lock:
-        c = _checks.get((word.device.index, word.data_ptr()))
-        return c is None or not c.pending
+    c = _checks.get((word.device.index, word.data_ptr()))
+    return c is None or not c.pending
 
 
-def _copy_after_call(word: torch.Tensor, stream: torch.cuda.Stream, tag: int = 0,
-                     speeds: "SmSpeeds | None" = None) -> None:
-    """Queue a copy of ``word`` to pinned host memory behind the work on
-    ``stream`` (on a side stream, so ``stream`` is not held up).  While one copy
-    is in flight no other is queued: the word keeps its bits until read, so the
-    next copy covers every call since.  After a call tagged ``tag`` the copy
-    also takes the call's per-SM timing records, for ``speeds``."""
+def _copy_after_call(word: torch.Tensor, stream_ptr: int, tag: int = 0, speeds: "SmSpeeds | None" = None) -> None:
+    """Queue a copy of ``word`` to pinned host memory behind the work on the
+    stream ``stream_ptr`` (on a side stream, so that stream is not held up).
+    While one copy is in flight no other is queued: the word keeps its bits
+    until read, so the next copy covers every call since.  After a call tagged
+    ``tag`` the copy also takes the call's per-SM timing records, for
+    ``speeds``."""
+    rt = _lib.cudart()
+    if rt is None:
+        return  # no runtime to queue the copy with: the synchronous checks still work
     key = (word.device.index, word.data_ptr())
     with _checks_lock:
         c = _checks.get(key)
         if c is None:
             if len(_checks) >= 64:
                 _checks.pop(next(iter(_checks)))
-            c = _checks[key] = _PendingCheck(word.device)
+            c = _checks[key] = _PendingCheck(word.device, rt)
         if c.pending:
             return
-        c.after_call.record(stream)
-        c.stream.wait_event(c.after_call)
         nbytes = 4
         if tag and speeds is not None and word.numel() >= _lib.PA_WS_SM_TIMING_OFFSET + speeds.n * 32:
             nbytes = _lib.PA_WS_SM_TIMING_OFFSET + speeds.n * _TIMING_DTYPE.itemsize
             c.tag, c.speeds = tag, speeds
-        with torch.cuda.stream(c.stream):
-            c.host[:nbytes].copy_(word[:nbytes], non_blocking=True)
-        word.record_stream(c.stream)  # a replaced workspace stays allocated until the copy has run
-        c.landed.record(c.stream)
+        if (rt.cudaEventRecord(c.ev_call, stream_ptr) or rt.cudaStreamWaitEvent(c.side_ptr, c.ev_call, 0)
+                or rt.cudaMemcpyAsync(c.host_ptr, word.data_ptr(), nbytes, 2, c.side_ptr)  # device to host
+                or rt.cudaEventRecord(c.ev_landed, c.side_ptr)):
+            raise RuntimeError("queueing the error-word copy failed")
+        c.word = word
         c.pending = True
 
 
 def _cache_view(t: torch.Tensor) -> CacheView:
-    return CacheView(t.data_ptr(), t.shape[0], t.stride(0), t.stride(1), t.stride(2))
+    st = t.stride()
+    return CacheView(t.data_ptr(), t.shape[0], st[0], st[1], st[2])
 
 
 def _check_cache_pair(key_cache: torch.Tensor, value_cache: torch.Tensor) -> None:
@@ -446,9 +474,9 @@ def kv_append(
     _check_new_rows(value, "value", B, Hkv, q_len, Dc, key_cache.dtype, device)
     args = KvAppendArgs()
     args.key = key.data_ptr()
-    args.key_stride_b, args.key_stride_h, args.key_stride_t = key.stride(0), key.stride(1), key.stride(2)
+    args.key_stride_b, args.key_stride_h, args.key_stride_t = key.stride()[:3]
     args.value = value.data_ptr()
-    args.value_stride_b, args.value_stride_h, args.value_stride_t = value.stride(0), value.stride(1), value.stride(2)
+    args.value_stride_b, args.value_stride_h, args.value_stride_t = value.stride()[:3]
     args.key_cache = _cache_view(key_cache)
     args.value_cache = _cache_view(value_cache)
     keep = []
@@ -493,7 +521,7 @@ def kv_append(
     with _with_device(device):
         _lib.check(_lib.load().pa_kv_append(ctypes.byref(args), _stream_ptr(device)), "pa_kv_append")
     if deferred:
-        _copy_after_call(error_word, torch.cuda.current_stream(device))
+        _copy_after_call(error_word, _stream_ptr(device))
     elif validate if validate is not None else _VALIDATE_DEFAULT:
         flags = read_device_errors(workspace=error_word)
         if flags:
@@ -593,6 +621,7 @@ def paged_attention_decode(
     deferred = validate is None and not _VALIDATE_DEFAULT and not _capturing()
     if deferred:
         _raise_landed_errors(workspace)
+    stream_ptr = _stream_ptr(device)
 
     appended = False
     if key is not None:
@@ -606,7 +635,7 @@ def paged_attention_decode(
 
     args = DecodeArgs()
     args.query = query.data_ptr()
-    args.query_stride_b, args.query_stride_h, args.query_stride_t = query.stride(0), query.stride(1), query.stride(2)
+    args.query_stride_b, args.query_stride_h, args.query_stride_t = query.stride()[:3]
     args.key_cache = _cache_view(key_cache)
     args.value_cache = _cache_view(value_cache)
     args.block_tables = block_tables.data_ptr()
@@ -615,7 +644,7 @@ def paged_attention_decode(
     args.context_lens = context_lens.data_ptr()
     args.len_offset = 0 if context_lens_include_new else q_len
     args.out = out.data_ptr()
-    args.out_stride_b, args.out_stride_h, args.out_stride_t = out.stride(0), out.stride(1), out.stride(2)
+    args.out_stride_b, args.out_stride_h, args.out_stride_t = out.stride()[:3]
     args.batch, args.q_len, args.num_q_heads, args.num_kv_heads = B, q_len, Hq, Hkv
     args.head_dim, args.block_size = D, bs
     args.dtype = dcode
@@ -634,16 +663,16 @@ def paged_attention_decode(
             args.sm_timing_tag = tag
     with _with_device(device):
         if gather is not None:
-            _lib.check(lib.pa_decode_gather(ctypes.byref(args), ctypes.byref(gather), _stream_ptr(device)),
+            _lib.check(lib.pa_decode_gather(ctypes.byref(args), ctypes.byref(gather), stream_ptr),
                        "pa_decode_gather")
         elif cascade:
             groups = prefix_groups.to_args()
-            _lib.check(lib.pa_decode_cascade(ctypes.byref(args), ctypes.byref(groups), _stream_ptr(device)),
+            _lib.check(lib.pa_decode_cascade(ctypes.byref(args), ctypes.byref(groups), stream_ptr),
                        "pa_decode_cascade")
         else:
-            _lib.check(lib.pa_decode(ctypes.byref(args), _stream_ptr(device)), "pa_decode")
+            _lib.check(lib.pa_decode(ctypes.byref(args), stream_ptr), "pa_decode")
     if deferred:
-        _copy_after_call(workspace, torch.cuda.current_stream(device), tag, speeds)
+        _copy_after_call(workspace, stream_ptr, tag, speeds)
     elif validate if validate is not None else _VALIDATE_DEFAULT:
         flags = read_device_errors(workspace=workspace)
         if flags:

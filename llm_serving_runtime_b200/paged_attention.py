@@ -430,6 +430,8 @@ class _with_device:
 
 
 _ws_bytes_cache: dict[tuple, int] = {}
+# pa_decode's message for a batch beyond its per-sequence shared-memory tables
+_BATCH_LIMIT_TEXT = "too large for the decode kernel's shared memory"
 
 
 def _workspace_bytes(B: int, Hq: int, Hkv: int, q_len: int, D: int, dcode: int, dev_index: int) -> int:
@@ -670,7 +672,19 @@ def paged_attention_decode(
             _lib.check(lib.pa_decode_cascade(ctypes.byref(args), ctypes.byref(groups), stream_ptr),
                        "pa_decode_cascade")
         else:
-            _lib.check(lib.pa_decode(ctypes.byref(args), stream_ptr), "pa_decode")
+            rc = lib.pa_decode(ctypes.byref(args), stream_ptr)
+            if rc == _lib.PA_ERR_UNSUPPORTED and B > 1 and _BATCH_LIMIT_TEXT in _lib.last_error():
+                # More sequences than the kernel's shared-memory tables hold:
+                # the rows are independent, so attend the two halves one after
+                # the other (the append above already covered every row).
+                half = B // 2
+                for lo, hi in ((0, half), (half, B)):
+                    paged_attention_decode(query[lo:hi], key_cache, value_cache, block_tables[lo:hi],
+                                           context_lens[lo:hi], scale, out=out[lo:hi],
+                                           context_lens_include_new=context_lens_include_new,
+                                           workspace=workspace, validate=False)
+            else:
+                _lib.check(rc, "pa_decode")
     if deferred:
         _copy_after_call(workspace, stream_ptr, tag, speeds)
     elif validate if validate is not None else _VALIDATE_DEFAULT:

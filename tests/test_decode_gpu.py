@@ -255,6 +255,24 @@ def test_many_short_sequences_and_large_batch():
     assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"
 
 
+def test_batch_beyond_the_shared_memory_tables_is_split():
+    # 9000 sequences at head_dim 128: more than the decode kernel's per-sequence
+    # shared-memory tables hold (about 8.3 k), so the call attends the batch in
+    # halves; the append covers every row in one launch first.
+    B = 9000
+    lens = torch.randint(0, 40, (B,), generator=torch.Generator().manual_seed(12)).tolist()
+    q, kc, vc, bt, cl = _synthetic(B, 8, 2, 128, 16, torch.bfloat16, lens, seed=13)
+    nk = (torch.randn(B, 2, 1, 128, generator=torch.Generator().manual_seed(14)) * 0.5).to(torch.bfloat16)
+    nv = (torch.randn(B, 2, 1, 128, generator=torch.Generator().manual_seed(15)) * 0.5).to(torch.bfloat16)
+    kcd, vcd = kc.to(DEV), vc.to(DEV)
+    out = paged_attention_decode(q.to(DEV), kcd, vcd, bt.to(DEV), cl.to(DEV), 128 ** -0.5, None, nk.to(DEV),
+                                 nv.to(DEV), validate=True)
+    oracle.write_tokens_batch(kc.unsqueeze(1), vc.unsqueeze(1), 0, bt, cl.long(), nk, nv)
+    assert torch.equal(kcd.cpu(), kc) and torch.equal(vcd.cpu(), vc)
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, 128 ** -0.5)
+    assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"
+
+
 def test_strided_pool_layer_view_and_transposed_query():
     # GpuKVBlockPool layout [num_blocks, layers, Hkv, bs, D]; layer 1 of 3; query
     # as HF produces it ([B, q, H, D] transposed to [B, H, q, D]).

@@ -20,7 +20,7 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libpa_b200.so"
 
 SOURCES = ["pa_capi.cu", "pa_kv_append.cu", "pa_decode_mma.cu", "pa_decode_f32.cu", "pa_static_ws.cu",
-           "pa_prefill_mma.cu", "pa_prefill_umma.cu"]
+           "pa_prefill_mma.cu", "pa_prefill_umma.cu", "pa_prefill_umma2.cu"]
 HEADERS = ["pa_common.cuh", "pa_internal.h", "pa_tile_math.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

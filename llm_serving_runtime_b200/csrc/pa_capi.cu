@@ -150,12 +150,18 @@ int encode_cache_map(CUtensorMap* map, const pa_cache_view& v, int dtype, int D,
 
 // Kernel choice for multi-query tiles: PA_B200_MULTIQUERY=mma forces the
 // mma.sync kernel (comparison / fallback); default is the tcgen05 kernel.
-constexpr int kPolicyAuto = 0, kPolicyMma = 1;
+// PA_B200_MULTIQUERY: "mma" (the mma.sync kernel), "umma" (the one-SM tcgen05
+// kernel), "umma2" (the SM-pair tcgen05 kernel where it applies); unset: auto.
+constexpr int kPolicyAuto = 0, kPolicyMma = 1, kPolicyUmma = 2, kPolicyUmma2 = 3;
 int multiquery_policy() {
   static int policy = -1;
   if (policy < 0) {
     const char* v = getenv("PA_B200_MULTIQUERY");
-    policy = (v != nullptr && strcmp(v, "mma") == 0) ? kPolicyMma : kPolicyAuto;
+    policy = v == nullptr                ? kPolicyAuto
+             : strcmp(v, "mma") == 0     ? kPolicyMma
+             : strcmp(v, "umma") == 0    ? kPolicyUmma
+             : strcmp(v, "umma2") == 0   ? kPolicyUmma2
+                                         : kPolicyAuto;
   }
   return policy;
 }
@@ -662,7 +668,14 @@ static int decode_impl(const pa_decode_args* a, const pa_prefix_groups* grp, con
     return PA_OK;
   }
   if (p.GQ >= 64 && prefill_tiles >= info->num_sms) {
-    if (rows16 && multiquery_policy() != kPolicyMma) {
+    const int pol = multiquery_policy();
+    // SM pairs (cta_group::2): head_dim 128, blocks of 16 tokens or more.
+    const bool pair_ok = rows16 && D == 128 && bs >= 16;
+    if (pair_ok && pol == kPolicyUmma2) {
+      g_last_kernel = "pa::prefill_umma2_kernel";
+      e = pa::launch_prefill_umma2(p, tmk, tmv, dtype, pdl, strm);
+      if (e != cudaSuccess) return cuda_fail(e, "tcgen05 SM-pair multi-query launch");
+    } else if (rows16 && pol != kPolicyMma) {
       g_last_kernel = "pa::prefill_umma_kernel";
       e = pa::launch_prefill_umma(p, tmk, tmv, dtype, pdl, strm);
       if (e != cudaSuccess) return cuda_fail(e, "tcgen05 multi-query launch");

@@ -151,6 +151,10 @@ cudaError_t launch_prefill_mma(const DecodeParams& p, const CUtensorMap& tmk, co
                                bool pdl, cudaStream_t stream);
 cudaError_t launch_prefill_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
                                 bool pdl, cudaStream_t stream);
+// The same on pairs of SMs (tcgen05 cta_group::2, clusters of 2 CTAs): head_dim
+// 128 (p.D), block_size >= 16 only.
+cudaError_t launch_prefill_umma2(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,
+                                 bool pdl, cudaStream_t stream);
 // Prefix part of pa_decode_cascade (tcgen05): one CTA per (split, group, kv head,
 // 128-row tile of the group's member rows).
 cudaError_t launch_prefix_umma(const DecodeParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int dtype,

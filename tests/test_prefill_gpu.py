@@ -78,3 +78,30 @@ def test_mma_multi_query_kernel_on_unaligned_output(B, Hq, Hkv, D, bs, dtype, le
     assert _lib.last_kernel() == "pa::prefill_mma_kernel"
     ref = oracle.paged_decode(q, kc, vc, bt, cl, D ** -0.5)
     assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"
+
+
+def test_sm_pair_kernel_passes_the_same_cases():
+    """The SM-pair tcgen05 kernel (cta_group::2, opt-in: PA_B200_MULTIQUERY=umma2)
+    on this file's cases, in a child process (the library reads the policy
+    once): every head_dim-128 case with 16-token or larger blocks takes it."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parent
+    env = dict(os.environ, PA_B200_MULTIQUERY="umma2")
+    probe = ("import sys, torch; sys.path[:0] = ['.', 'tests']\n"
+             "from llm_serving_runtime_b200 import paged_attention_decode, _lib\n"
+             "from llm_serving_runtime_b200.workloads import make_workload\n"
+             "w = make_workload('prefill-llama3-8b', device='cuda')\n"
+             "paged_attention_decode(w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)\n"
+             "torch.cuda.synchronize(); print(_lib.last_kernel())\n")
+    kernel = subprocess.run([sys.executable, "-c", probe], cwd=here.parent, env=env, capture_output=True, text=True,
+                            timeout=600)
+    assert kernel.returncode == 0, kernel.stderr[-2000:]
+    assert kernel.stdout.strip().endswith("pa::prefill_umma2_kernel")
+    run = subprocess.run([sys.executable, "-m", "pytest", str(here / "test_prefill_gpu.py"), "-q", "-x",
+                          "-p", "no:cacheprovider", "-k", "multi_query_chunks or prefill_workload"],
+                         cwd=here.parent, env=env, capture_output=True, text=True, timeout=1200)
+    assert run.returncode == 0, run.stdout[-3000:]

@@ -232,8 +232,9 @@ def cudart() -> ctypes.CDLL | None:
         rt.cudaStreamWaitEvent.argtypes = [_vp, _vp, ctypes.c_uint]
         rt.cudaMemcpyAsync.argtypes = [_vp, _vp, _sz, ctypes.c_int, _vp]
         rt.cudaEventQuery.argtypes = [_vp]
+        rt.cudaEventDestroy.argtypes = [_vp]
         for f in (rt.cudaEventCreateWithFlags, rt.cudaEventRecord, rt.cudaStreamWaitEvent, rt.cudaMemcpyAsync,
-                  rt.cudaEventQuery):
+                  rt.cudaEventQuery, rt.cudaEventDestroy):
             f.restype = ctypes.c_int
         _cudart_handle = rt
         return rt

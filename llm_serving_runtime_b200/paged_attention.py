@@ -354,7 +354,17 @@ def _copy_after_call(word: torch.Tensor, stream_ptr: int, tag: int = 0, speeds: 
         c = _checks.get(key)
         if c is None:
             if len(_checks) >= 64:
-                _checks.pop(next(iter(_checks)))
+                # drop the oldest entry whose copy is not in flight (its pinned
+                # buffer may then be freed; a landed but unread error stays in
+                # the device word, which only a read clears, so the workspace's
+                # next call reports it); with every copy in flight, skip this check
+                idle = next((k for k, v in _checks.items()
+                             if not v.pending or rt.cudaEventQuery(v.ev_landed) == 0), None)
+                if idle is None:
+                    return
+                old = _checks.pop(idle)
+                rt.cudaEventDestroy(old.ev_call)
+                rt.cudaEventDestroy(old.ev_landed)
             c = _checks[key] = _PendingCheck(word.device, rt)
         if c.pending:
             return

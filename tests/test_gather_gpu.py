@@ -20,7 +20,7 @@ import pytest
 import torch
 
 from llm_serving_runtime_b200 import _lib, paged_attention_decode, read_device_errors
-from llm_serving_runtime_b200.paged_attention import DeviceErrorFlags
+from llm_serving_runtime_b200.paged_attention import DeviceErrorFlags, decode_workspace
 from llm_serving_runtime_b200.workloads import SPECS, make_workload
 
 pytestmark = pytest.mark.gpu
@@ -126,6 +126,33 @@ def test_bad_block_id_raises_at_the_next_call_without_validate():
     good = paged_attention_decode(*args)
     torch.cuda.synchronize()
     assert torch.equal(paged_attention_decode(*args), good)
+
+
+def test_an_error_outlives_the_check_table_eviction():
+    """More workspaces than the table of deferred checks holds: the entry of
+    the failing call's workspace is dropped on the way, but its device word
+    keeps the error bits, so the workspace's next calls still raise."""
+    w = _workload(batch=8)
+    args = (w.query, w.key_cache, w.value_cache, w.block_tables, w.context_lens, w.scale)
+    paged_attention_decode(*args)
+    nbytes = decode_workspace(DEV).numel()
+    spaces = [torch.zeros(nbytes, dtype=torch.uint8, device=DEV) for _ in range(130)]
+    good = paged_attention_decode(*args, workspace=spaces[1])
+    bad = w.block_tables.clone()
+    bad[2, 0] = w.key_cache.shape[0] + 3
+    paged_attention_decode(w.query, w.key_cache, w.value_cache, bad, w.context_lens, w.scale,
+                           workspace=spaces[0])  # returns; the error lands in spaces[0]
+    torch.cuda.synchronize()
+    for ws in spaces[1:]:
+        assert torch.allclose(paged_attention_decode(*args, workspace=ws), good, rtol=0, atol=2e-3)
+    torch.cuda.synchronize()
+    with pytest.raises(IndexError, match="out of range"):
+        for _ in range(2):  # the first call raises if the entry survived, else the second
+            paged_attention_decode(*args, workspace=spaces[0])
+            torch.cuda.synchronize()
+    assert read_device_errors(workspace=spaces[0]) == 0
+    torch.cuda.synchronize()
+    assert torch.allclose(paged_attention_decode(*args, workspace=spaces[0]), good, rtol=0, atol=2e-3)
 
 
 def _free_port() -> int:

@@ -104,6 +104,24 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// L2 policy for data read once: its lines are the first to go, so a stream of
+// them does not push out what is read again (queries, partial states, tables).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// tma_load_4d with an L2 cache policy (l2_policy_evict_first).
+__device__ __forceinline__ void tma_load_4d_policy(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                   int x, int y, int z, int w, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w), "l"(pol)
+      : "memory");
+}
+
 // 4-byte asynchronous global -> shared copy (no register round trip), and the
 // wait for all of this thread's outstanding ones.
 __device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {

@@ -537,6 +537,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     }
   };
 
+  // The K/V stream is read once: evict-first keeps it from pushing the query
+  // rows, partial states, prefix states and tables out of L2.
+  const uint64_t kv_policy = l2_policy_evict_first();
   auto issue = [&](int slot) {
     const int h = pc.h;
     if constexpr (cascade) {
@@ -555,10 +558,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
         mbar_arrive_expect_tx(bar, STAGE_BYTES);
 #pragma unroll
         for (int hf = 0; hf < HALVES; ++hf)
-          tma_load_4d(stage + hf * 2048u, &tmk, bar, hf * 64, y, h, phys);
+          tma_load_4d_policy(stage + hf * 2048u, &tmk, bar, hf * 64, y, h, phys, kv_policy);
 #pragma unroll
         for (int hf = 0; hf < HALVES; ++hf)
-          tma_load_4d(stage + TILE_BYTES + hf * 2048u, &tmv, bar, hf * 64, y, h, phys);
+          tma_load_4d_policy(stage + TILE_BYTES + hf * 2048u, &tmv, bar, hf * 64, y, h, phys, kv_policy);
       }
     } else {
       // Block size 8: two blocks per unit; a block past the sequence end is not loaded.
@@ -578,9 +581,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           const int phys = j ? phys1 : phys0;
 #pragma unroll
           for (int hf = 0; hf < HALVES; ++hf) {
-            tma_load_4d(stage + hf * 2048u + j * box_bytes, &tmk, bar, hf * 64, 0, h, phys);
-            tma_load_4d(stage + TILE_BYTES + hf * 2048u + j * box_bytes, &tmv, bar, hf * 64, 0, h,
-                        phys);
+            tma_load_4d_policy(stage + hf * 2048u + j * box_bytes, &tmk, bar, hf * 64, 0, h, phys, kv_policy);
+            tma_load_4d_policy(stage + TILE_BYTES + hf * 2048u + j * box_bytes, &tmv, bar, hf * 64, 0, h,
+                               phys, kv_policy);
           }
         }
       }

@@ -514,16 +514,30 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
       lim = Lb - p.q_len + tq;
       if constexpr (kPrefix) lim = min(lim, kv_end - 1);
     }
-    // Q row -> swizzled K-major tile t (row r)
+    // Q rows -> swizzled K-major tile t.  The warp loads its 32 rows together,
+    // whole rows per instruction (a row's 16-byte pieces from consecutive
+    // lanes), so each load touches a few full lines instead of one line per lane.
     {
       const T* qrow = static_cast<const T*>(p.q) + (long long)b * p.q_sb + (long long)(h * p.G + g) * p.q_sh +
                       (long long)tq * p.q_st;
       uint8_t* qt = s_q + t * QT_BYTES;
+      constexpr int CH = D / 8;     // 16-byte pieces per row
+      constexpr int RPI = 32 / CH;  // rows per warp instruction
+      const int sub = lane / CH, c = lane % CH;
+      const unsigned long long my_row = reinterpret_cast<unsigned long long>(qrow);
+      uint4 v[32 / RPI];
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (row_ok && c * 8 < p.Dv) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        *reinterpret_cast<uint4*>(qt + (c >> 3) * 16384 + sw128_chunk(r, c & 7)) = v;
+      for (int k = 0; k < 32 / RPI; ++k) {
+        const int src = k * RPI + sub;  // the lane whose row this is
+        const T* rp = reinterpret_cast<const T*>(__shfl_sync(0xffffffffu, my_row, src));
+        const bool rok = __shfl_sync(0xffffffffu, (int)row_ok, src) != 0;
+        v[k] = make_uint4(0u, 0u, 0u, 0u);
+        if (rok && c * 8 < p.Dv) v[k] = *reinterpret_cast<const uint4*>(rp + c * 8);
+      }
+#pragma unroll
+      for (int k = 0; k < 32 / RPI; ++k) {
+        const int rr = (warp & 3) * 32 + k * RPI + sub;  // row within the tile
+        *reinterpret_cast<uint4*>(qt + (c >> 3) * 16384 + sw128_chunk(rr, c & 7)) = v[k];
       }
     }
     fence_proxy_async_smem();
@@ -652,21 +666,60 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
                              ((long long)b * p.Hq + h * p.G + g) * p.q_len + tq;
       if (row_ok) p.pre_ml[ridx] = make_float2(have ? m_ref : -INFINITY, have ? l : 0.f);
       float* arow = p.pre_acc + ridx * D;
+      // The warp's 32 rows go out through shared memory, whole rows per store
+      // instruction.  Staging space: tile 0 the Q tiles, tile 1 the K/V ring.
+      // Both are free once this tile's last P.V has completed: its commit
+      // tracks every MMA issued before it, and tile 1's last P.V is the last
+      // MMA.  Without a clean finish (a wait ran out, copies may still be in
+      // flight) the rows go out one per thread.
+      const bool staged = tile_on && __all_sync(0xffffffffu, ok) && __any_sync(0xffffffffu, row_ok);
+      if (staged) {
+        constexpr int CHF = D / 4;  // 16-byte pieces per fp32 row
+        uint8_t* sw = (t == 0 ? s_q : s_kv) + (warp & 3) * (32 * D * 4);
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t o[32];
-        if (have_o) {
-          tmem_ld32(t_o + c0, o);
-          tmem_wait_ld();
-        }
-        if (row_ok) {
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          if (have_o) {
+            tmem_ld32(t_o + c0, o);
+            tmem_wait_ld();
+          }
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (have)
-              v = make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]),
-                              __uint_as_float(o[i + 3]));
-            *reinterpret_cast<float4*>(arow + c0 + i) = v;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (have) v = make_uint4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+            const int piece = (c0 + i) / 4;
+            *reinterpret_cast<uint4*>(sw + lane * (D * 4) + ((piece ^ lane) & (CHF - 1)) * 16) = v;
+          }
+        }
+        __syncwarp();
+        constexpr int RPI = 32 / CHF;  // rows per store instruction
+        const int sub = lane / CHF, pc = lane % CHF;
+        const unsigned long long my_row = reinterpret_cast<unsigned long long>(arow);
+#pragma unroll 4
+        for (int k = 0; k < 32 / RPI; ++k) {
+          const int src = k * RPI + sub;
+          float* dst = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, my_row, src));
+          const bool rok = __shfl_sync(0xffffffffu, (int)row_ok, src) != 0;
+          const uint4 v = *reinterpret_cast<const uint4*>(sw + src * (D * 4) + ((pc ^ src) & (CHF - 1)) * 16);
+          if (rok) *reinterpret_cast<uint4*>(dst + pc * 4) = v;
+        }
+      } else {
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          if (have_o) {
+            tmem_ld32(t_o + c0, o);
+            tmem_wait_ld();
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (have)
+                v = make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]),
+                                __uint_as_float(o[i + 3]));
+              *reinterpret_cast<float4*>(arow + c0 + i) = v;
+            }
           }
         }
       }
@@ -717,26 +770,68 @@ __global__ void __launch_bounds__(umma_threads(kPrefix), 1)
       T* orow = static_cast<T*>(p.out) + (long long)b * p.o_sb + (long long)(h * p.G + g) * p.o_sh +
                 (long long)tq * p.o_st;
       const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
+      // As in the prefix epilogue: the warp's rows go out through shared
+      // memory (this tile's Q tile, free once its last P.V has completed),
+      // whole rows per store instruction.
+      const bool staged = tile_on && __all_sync(0xffffffffu, ok) && __any_sync(0xffffffffu, row_ok);
+      if (staged) {
+        constexpr int CHB = D / 8;  // 16-byte pieces per output row
+        uint8_t* sw = s_q + t * QT_BYTES + (warp & 3) * (32 * D * 2);
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t o[32];
-        if (have_o) {
-          tmem_ld32(t_o + c0, o);
-          tmem_wait_ld();
-        } else {
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          if (have_o) {
+            tmem_ld32(t_o + c0, o);
+            tmem_wait_ld();
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0u;
-        }
-        if (row_ok) {
+            for (int i = 0; i < 32; ++i) o[i] = 0u;
+          }
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
-            if (c0 + i >= p.Dv) break;  // columns past the head_dim
             uint4 v;
             v.x = pack2<T>(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
             v.y = pack2<T>(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
             v.z = pack2<T>(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
             v.w = pack2<T>(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c0 + i) = v;
+            const int piece = (c0 + i) / 8;
+            *reinterpret_cast<uint4*>(sw + lane * (D * 2) + ((piece ^ lane) & (CHB - 1)) * 16) = v;
+          }
+        }
+        __syncwarp();
+        constexpr int RPI = 32 / CHB;  // rows per store instruction
+        const int sub = lane / CHB, pc = lane % CHB;
+        const unsigned long long my_row = reinterpret_cast<unsigned long long>(orow);
+#pragma unroll 4
+        for (int k = 0; k < 32 / RPI; ++k) {
+          const int src = k * RPI + sub;
+          T* dst = reinterpret_cast<T*>(__shfl_sync(0xffffffffu, my_row, src));
+          const bool rok = __shfl_sync(0xffffffffu, (int)row_ok, src) != 0;
+          const uint4 v = *reinterpret_cast<const uint4*>(sw + src * (D * 2) + ((pc ^ src) & (CHB - 1)) * 16);
+          if (rok && pc * 8 < p.Dv) *reinterpret_cast<uint4*>(dst + pc * 8) = v;
+        }
+      } else {
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          if (have_o) {
+            tmem_ld32(t_o + c0, o);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = 0u;
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              if (c0 + i >= p.Dv) break;  // columns past the head_dim
+              uint4 v;
+              v.x = pack2<T>(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
+              v.y = pack2<T>(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+              v.z = pack2<T>(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+              v.w = pack2<T>(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c0 + i) = v;
+            }
           }
         }
       }

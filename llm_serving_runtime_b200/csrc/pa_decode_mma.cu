@@ -301,16 +301,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
   };
   if constexpr (!cascade) fill_empty_rows();
 
-  // Everything below reads the KV cache, which the previous kernel may write
-  // (and, under the cascade, the prefix states the previous kernel leaves).
-  pdl_wait_previous();
-  if constexpr (cascade) fill_empty_rows();
-
+  // Up to the first K/V load, the slices below read only the lengths and the
+  // block tables, which the previous kernel (the append, or under the cascade
+  // the prefix pass) does not write: they are worked out, and each warp's
+  // first block-table window loaded, before waiting for that kernel.
   const long long W = s_pref[B];
-  if (W == 0) {
-    finish_warp();
-    return;
-  }
   // Slices are equal in cost, not in units: a row (a row group of one
   // sequence and kv head with units) costs its units plus kRowCostUnits for
   // what a row start and end take (query load, output store, fold, merge).
@@ -401,13 +396,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       }
     }
   };
-  if (weighted && s_slot < 0) {  // cannot happen (one CTA per slot); leave the work undone and say so
-    if (lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
-    leave_weighted();
-    finish_warp();
-    return;
-  }
-  if (weighted && lane == 0) atomicMin(&s_t0, (unsigned long long)global_ns());
+  const bool slot_ok = !(weighted && s_slot < 0);  // always (one CTA per slot)
   auto cost_pref = [&](int b) -> long long { return (long long)s_pref[b] + (long long)kRowCostUnits * s_rpref[b]; };
   // Cost at which row group mg of kv head h of sequence b starts.
   auto row_cost_start = [&](int b, int h, int mg) -> long long {
@@ -448,19 +437,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     }
     return f;
   };
-  const long long ws = unit_at_cost(warp_start(gw));
-  const long long we = unit_at_cost(warp_start(gw + 1));
-  if (gw >= nw_eff || ws >= we) {
-    leave_weighted();
-    finish_warp();
-    return;
-  }
+  const long long ws = slot_ok ? unit_at_cost(warp_start(gw)) : 0;
+  const long long we = slot_ok ? unit_at_cost(warp_start(gw + 1)) : 0;
+  const bool has_work = slot_ok && W > 0 && gw < nw_eff && ws < we;
 
   // Locate the first unit of this warp's slice.
   // Flat order: sequence, then kv head, then row group, then unit; a sequence
   // spans Hkv * S_b units with S_b the units of its row groups.
-  Cursor start;
-  {
+  Cursor start = {0, 0, 0, 0, 0};
+  if (has_work) {
     int lo = 0, hi = B - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
@@ -589,6 +574,28 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       }
     }
   };
+
+  if (has_work) {
+    const int tok0 = (start.u + (cascade ? s_u0[start.b] : 0)) * kUnitTokens;
+    ensure_window(start.b, tok0 / bs, bs >= kUnitTokens ? 1 : 2);
+  }
+
+  // Everything below reads the K/V cache, which the previous kernel may write
+  // (and, under the cascade, the prefix states the previous kernel leaves).
+  pdl_wait_previous();
+  if constexpr (cascade) fill_empty_rows();
+  if (!slot_ok) {  // leave the work undone and say so
+    if (lane == 0) raise_flag(p.status, PA_DEVERR_WAIT_TIMEOUT);
+    leave_weighted();
+    finish_warp();
+    return;
+  }
+  if (weighted && lane == 0) atomicMin(&s_t0, (unsigned long long)global_ns());
+  if (!has_work) {
+    leave_weighted();
+    finish_warp();
+    return;
+  }
 
   for (int s = 0; s < stages && pf < we; ++s) {
     issue(s);

@@ -52,6 +52,26 @@ def test_multi_query_chunks_vs_oracle(B, Hq, Hkv, D, bs, dtype, lens, q_len):
     assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"
 
 
+@pytest.mark.parametrize("D", [128, 64])
+def test_bf16_values_far_beyond_fp16_range(D):
+    """bf16 caches holding values fp16 cannot (up to 3e5, and 65280 / 65536
+    at the edge of fp16's range) on the tcgen05 multi-query kernel: P is split
+    into two bf16 parts, so the products keep ~16 bits of it at any scale."""
+    B, Hq, Hkv, bs, q_len = 10, 32, 8, 16, 256
+    lens = [0, 50, 300, 1000, 17, 0, 2000, 64, 5, 700]
+    q, kc, vc, bt, cl = _synthetic(B, Hq, Hkv, D, bs, torch.bfloat16, lens, q_len, seed=77 + D)
+    v = vc.float()
+    v[::3, :, 5, 7] = 3.0e5
+    v[1::7, :, 2, 1] = -65536.0
+    v[2::5, :, 9, 3] = 65280.0
+    v[4::9, :, 11, 0] = -65280.0
+    vc = v.to(torch.bfloat16)
+    out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), D ** -0.5,
+                                 validate=True)
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, D ** -0.5)
+    assert excess_err(out, ref) <= 0, f"max abs err {max_err(out, ref)}"
+
+
 def test_prefill_workload_with_append_sampled_rows():
     from _util import oracle_rows
 

@@ -179,6 +179,16 @@ def _two_rank_worker(rank: int, port: int) -> None:
             a = fused(*args).clone()
             b = nccl(*args)
             assert torch.equal(a, b), f"rank {rank}: fused gather differs from the NCCL all-gather"
+        # against the oracle: both ranks draw the same data for their own KV
+        # heads, so every rank's slice of the gathered output is that decode
+        from _util import TOL, max_err, oracle_rows
+
+        rows = [0, 5, 17, 31]
+        ref = oracle_rows(*args[:5], w.scale, w.q_len, rows)
+        hl = w.query.shape[1]
+        for r2 in range(2):
+            err = max_err(a[rows][:, r2 * hl:(r2 + 1) * hl], ref)
+            assert err <= TOL[torch.bfloat16], f"rank {rank}: slice of rank {r2} off the oracle by {err}"
         dest = torch.empty_like(b)
         assert fused(*args, out=dest) is dest and torch.equal(dest, b)
         # fp32 takes the NCCL form under the same call

@@ -164,3 +164,43 @@ def test_cascade_inside_a_cuda_graph():
         torch.cuda.synchronize()
         ref = oracle.paged_decode(q, kc, vc, bt, lens, 128 ** -0.5, len_offset=1)
         assert excess_err(out, ref) <= 0, f"step {grow}: max abs err {max_err(out, ref)}"
+
+
+def _random_cascade(seed):
+    import random
+
+    rnd = random.Random(seed)
+    dtype = rnd.choice([torch.bfloat16, torch.float16])
+    D = rnd.choice([64, 128, 128, 80])
+    bs = rnd.choice([8, 16, 16, 32, 64, 128])
+    Hkv = rnd.choice([1, 2, 8])
+    G = rnd.choice([1, 4, 4, 7, 8])
+    q_len = rnd.choice([1, 1, 2, 4])
+    n_groups = rnd.randint(1, 5)
+    groups = [rnd.randint(1, 12) for _ in range(n_groups)]
+    prefix_lens = [bs * rnd.randint(1, max(1, 1536 // bs)) for _ in range(n_groups)]
+    lone = rnd.randint(0, 4)
+    cached = []
+    for gi, size in enumerate(groups):
+        for _ in range(size):
+            # a member holds the whole prefix; its own part may be empty
+            cached.append(prefix_lens[gi] + rnd.choice([0, 0, rnd.randint(0, bs), rnd.randint(0, 900)]))
+    cached += [rnd.randint(0, 1500) for _ in range(lone)]
+    return groups, prefix_lens, lone, cached, G * Hkv, Hkv, D, bs, dtype, q_len
+
+
+@pytest.mark.parametrize("seed", range(80))
+def test_random_cascades_vs_oracle(seed):
+    """Seeded random groups (sizes, prefix lengths, members with empty or short
+    own parts, lone rows) over random shapes: the cascade, with the groups given
+    and with the groups found from the block tables, against the oracle."""
+    groups, prefix_lens, lone, cached, Hq, Hkv, D, bs, dtype, q_len = _random_cascade(seed)
+    q, kc, vc, bt, cl, members = _shared_batch(groups, prefix_lens, lone, cached, Hq, Hkv, D, bs, dtype, q_len,
+                                               seed=7000 + seed)
+    args = (q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV), D ** -0.5)
+    ref = oracle.paged_decode(q, kc, vc, bt, cl, D ** -0.5, len_offset=q_len)
+    given = PrefixGroups.from_members(members, prefix_lens, q.shape[0], DEV)
+    found = find_shared_prefixes(bt, cl, block_size=bs, min_shared_tokens=bs, device=DEV)
+    for pg in (given, found):
+        out = paged_attention_decode(*args, prefix_groups=pg, validate=True)
+        assert excess_err(out, ref) <= 0, f"seed {seed}: max abs err {max_err(out, ref)}"

@@ -125,3 +125,34 @@ def test_sm_pair_kernel_passes_the_same_cases():
                           "-p", "no:cacheprovider", "-k", "multi_query_chunks or prefill_workload"],
                          cwd=here.parent, env=env, capture_output=True, text=True, timeout=1200)
     assert run.returncode == 0, run.stdout[-3000:]
+
+
+def _random_multi_query(seed):
+    import random
+
+    rnd = random.Random(seed)
+    dtype = rnd.choice([torch.bfloat16, torch.float16])
+    D = rnd.choice([64, 128, 128, 80, 96])
+    bs = rnd.choice([8, 16, 16, 32, 64, 128])
+    Hkv = rnd.choice([4, 8, 8])
+    G = rnd.choice([4, 7, 8])
+    q_len = rnd.choice([64, 128, 160, 256])
+    B = rnd.randint(3, 10)
+    lens = [rnd.choice([0, rnd.randint(1, 64), rnd.randint(0, 1200)]) for _ in range(B)]
+    return B, G * Hkv, Hkv, D, bs, dtype, lens, q_len
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_random_multi_query_vs_oracle(seed):
+    """Seeded random chunked-prefill shapes, most of them with enough 128-row
+    tiles for the tcgen05 multi-query kernel, against the oracle on three rows
+    (the first, the last and the longest)."""
+    from _util import oracle_rows
+
+    B, Hq, Hkv, D, bs, dtype, lens, q_len = _random_multi_query(seed)
+    q, kc, vc, bt, cl = _synthetic(B, Hq, Hkv, D, bs, dtype, lens, q_len, seed=3000 + seed)
+    q, kc, vc, bt, cl = q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), cl.to(DEV)
+    out = paged_attention_decode(q, kc, vc, bt, cl, D ** -0.5, validate=True)
+    rows = sorted({0, B - 1, max(range(B), key=lambda b: lens[b])})
+    ref = oracle_rows(q, kc, vc, bt, cl, D ** -0.5, q_len, rows)
+    assert excess_err(out[rows], ref) <= 0, f"seed {seed}: max abs err {max_err(out[rows], ref)}"

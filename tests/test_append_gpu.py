@@ -142,3 +142,47 @@ def test_append_bit_exact_across_block_sizes(bs, D, dtype):
     derived = oracle.slot_mapping_from_tables(tables, starts, q_len, bs)
     oracle.kv_append(nk, nv, ref_k, ref_v, derived)
     assert torch.equal(_bits(kc_d), _bits(ref_k)) and torch.equal(_bits(vc_d), _bits(ref_v))
+
+
+def _random_append(seed):
+    import random
+
+    from test_decode_gpu import _synthetic
+
+    rnd = random.Random(seed)
+    dtype = rnd.choice([torch.bfloat16, torch.float16, torch.float32])
+    D = rnd.choice([rnd.randint(1, 160), 64, 128])
+    bs = rnd.choice([4, 8, 16, 16, 32, 64, 128, 256])
+    Hkv = rnd.randint(1, 8)
+    q_len = rnd.choice([1, 1, 2, 4, 8, 16])
+    B = rnd.randint(1, 30)
+    lens = [rnd.choice([0, rnd.randint(0, 3 * bs), rnd.randint(0, 2000)]) for _ in range(B)]
+    _, kc, vc, bt, cl = _synthetic(B, Hkv, Hkv, D, bs, dtype, lens, q_len, seed=5000 + seed)
+    g = torch.Generator().manual_seed(6000 + seed)
+    nk = torch.randn(B, Hkv, q_len, D, generator=g).to(dtype)
+    nv = torch.randn(B, Hkv, q_len, D, generator=g).to(dtype)
+    pos = cl.long()[:, None] + torch.arange(q_len)[None, :]
+    phys = torch.gather(bt.long(), 1, pos // bs)
+    slots = (phys * bs + pos % bs).reshape(-1)
+    pad = torch.rand(slots.shape, generator=g) < 0.1
+    return kc, vc, bt, cl, nk, nv, slots, torch.where(pad, torch.full_like(slots, -1), slots)
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_random_appends_bit_exact(seed):
+    """Seeded random appends (dtype, head_dim 1..160, block size, KV heads,
+    tokens per sequence, lengths; a tenth of the slots padding) through a slot
+    mapping and through block tables + positions, bit for bit against the
+    oracle's scatter."""
+    kc, vc, bt, cl, nk, nv, slots, padded = _random_append(seed)
+    for how in ("slots", "tables"):
+        kd, vd = kc.to(DEV), vc.to(DEV)
+        kr, vr = kc.clone(), vc.clone()
+        if how == "slots":
+            kv_append(nk.to(DEV), nv.to(DEV), kd, vd, padded.to(DEV), validate=True)
+            oracle.kv_append(nk, nv, kr, vr, padded)
+        else:
+            kv_append(nk.to(DEV), nv.to(DEV), kd, vd, block_tables=bt.to(DEV), positions=cl.to(DEV), validate=True)
+            oracle.kv_append(nk, nv, kr, vr, slots)
+        assert torch.equal(_bits(kd), _bits(kr)), f"seed {seed} ({how}): key cache differs"
+        assert torch.equal(_bits(vd), _bits(vr)), f"seed {seed} ({how}): value cache differs"
